@@ -1,0 +1,154 @@
+"""Pins the CPU oracle against the reference's own outputs (tests/golden/).
+
+The oracle (oracle/aw4_oracle.c) is the checker for every GPU parity test, so
+it is trusted only after matching what the reference produced on the same
+inputs: codebooks, codec cases (RTN, value-SR and update-SR given the
+reference's uniforms, EDEN, the zero floor and the scale floor) and optimizer
+trajectories.  Codes and block scales must be bit-exact; parameters must agree
+within rtol=1e-6 (the reference's CPU sqrt is MKL VML, not correctly rounded,
+so the denominator may differ by one ulp in rare elements).
+"""
+
+from __future__ import annotations
+
+import json
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle as O
+from tests import golden_io as G
+
+PARAM_RTOL = 1e-6
+PARAM_ATOL = 1e-9
+
+
+def test_codebooks_match_reference():
+    with open(os.path.join(G.GOLDEN, "codebooks.json")) as f:
+        ref = json.load(f)
+    for scheme, words in ref.items():
+        cb = O.SCHEMES[scheme][0]
+        assert [int(w) for w in cb.view(np.uint32)] == words, scheme
+
+
+def test_codec_cases_bit_exact():
+    with open(os.path.join(G.GOLDEN, "codec_cases.json")) as f:
+        meta = json.load(f)
+    arrays = np.load(os.path.join(G.GOLDEN, "codec_cases.npz"))
+    for case in meta:
+        tag, scheme = case["tag"], case["scheme"]
+        codes, scales = O.quantize(arrays[f"{tag}_x"], scheme, eden=case["eden"],
+                                   draws=arrays[f"{tag}_draws"],
+                                   bias_correction=case["bias_correction"], eps=case["eps"])
+        np.testing.assert_array_equal(codes, arrays[f"{tag}_codes"], err_msg=tag + scheme)
+        np.testing.assert_array_equal(scales.view(np.uint32),
+                                      arrays[f"{tag}_scales"].view(np.uint32), err_msg=tag)
+
+
+def test_nibble_order_kat():
+    """tests/quantization/test_utils.py:92-101 of the reference: [1,2,15] -> [0x21, 0x0F]."""
+    arrays = np.load(os.path.join(G.GOLDEN, "codec_cases.npz"))
+    np.testing.assert_array_equal(O.pack(arrays["pack_in"]), arrays["pack_out"])
+    np.testing.assert_array_equal(O.unpack(arrays["pack_out"], 3), arrays["pack_in"])
+
+
+def _np_param(t: torch.Tensor) -> np.ndarray:
+    if t.dtype == torch.float32:
+        return t.numpy().reshape(-1).copy()
+    return t.view(torch.int16).numpy().reshape(-1).view(np.uint16).copy()
+
+
+def _f32(a: np.ndarray, dtype: torch.dtype) -> np.ndarray:
+    if dtype == torch.float32:
+        return a
+    return torch.from_numpy(a.view(np.int16)).view(dtype).float().numpy()
+
+
+_DT = {torch.float32: O.F32, torch.bfloat16: O.BF16, torch.float16: O.F16}
+
+
+def run_oracle_trajectory(meta: dict, on_step=None):
+    """Run the oracle over a fixture's replayed inputs; yields per-step state."""
+    rep = G.Replay(meta)
+    params = [_np_param(p) for p in rep.init_params()]
+    state = []
+    for p, s in zip(params, rep.shapes):
+        n = int(np.prod(s))
+        if G.eligible(n):
+            c1, s1 = O.init_zero(rep.m1_scheme, n)
+            c2, s2 = O.init_zero(rep.m2_scheme, n, eden=rep.eden)
+            state.append({"m1_code": c1, "m1_absmax": s1, "m2_code": c2, "m2_absmax": s2})
+        else:
+            state.append({"m1": np.zeros(n, np.float32), "m2": np.zeros(n, np.float32)})
+    for t in range(1, meta["steps"] + 1):
+        inp = rep.next()
+        for i, (p, st) in enumerate(zip(params, state)):
+            g = _np_param(inp.grads[i])
+            m1_scheme = inp.m1_scheme if i == 0 else rep.m1_scheme
+            cfg = O.make_cfg(m1_scheme=m1_scheme, m2_scheme=rep.m2_scheme, eden=rep.eden,
+                             lr=meta["lr"], betas=meta["betas"], eps=meta["eps"],
+                             weight_decay=meta["weight_decay"], step=t,
+                             param_dtype=_DT[rep.p_dtype], grad_dtype=_DT[rep.g_dtype])
+            if "m1_code" in st:
+                O.step(cfg, p, g, st["m1_code"], st["m1_absmax"], st["m2_code"], st["m2_absmax"],
+                       inp.m1_draws[i], inp.m2_draws[i])
+            else:
+                O.step_fp32_state(cfg, p, g, st["m1"], st["m2"])
+        if on_step is not None:
+            on_step(t, inp, params, state)
+    return params, state
+
+
+TRAJS = ["zeeden_f32_small", "zipsr_f32_small", "zeeden_switch_small", "zipsr_bf16_outliers",
+         "zeeden_f32p_bf16g", "zeeden_f16"]
+
+
+@pytest.mark.parametrize("name", TRAJS)
+def test_oracle_trajectory_matches_reference(name):
+    meta, arrays = G.load_traj(name)
+    rep_dtype = G.DTYPES[meta["p_dtype"]]
+
+    def check(t, inp, params, state):
+        rec = meta["per_step"][t - 1]
+        for i, g in enumerate(inp.grads):
+            assert G.sha(g) == rec["grad_sha"][i], f"gradient recipe drifted at step {t}"
+        st = state[0]
+        for key in ("m1_code", "m1_absmax", "m2_code", "m2_absmax"):
+            assert G.sha_np(st[key]) == rec[key], f"{name} step {t} {key}"
+        sample = _f32(params[0], rep_dtype)[::meta["sample_stride"]]
+        np.testing.assert_allclose(sample, arrays[f"s{t}_param_sample"], rtol=PARAM_RTOL,
+                                   atol=PARAM_ATOL, err_msg=f"{name} step {t}")
+        if f"s{t}_param" in arrays:
+            np.testing.assert_allclose(_f32(params[0], rep_dtype), arrays[f"s{t}_param"],
+                                       rtol=PARAM_RTOL, atol=PARAM_ATOL)
+        for i in range(1, len(params)):
+            if f"s{t}_small{i}_param" in arrays:
+                np.testing.assert_allclose(_f32(params[i], rep_dtype),
+                                           arrays[f"s{t}_small{i}_param"], rtol=PARAM_RTOL,
+                                           atol=PARAM_ATOL)
+                np.testing.assert_allclose(state[i]["m1"], arrays[f"s{t}_small{i}_m1"],
+                                           rtol=0, atol=0)
+                np.testing.assert_allclose(state[i]["m2"], arrays[f"s{t}_small{i}_m2"],
+                                           rtol=0, atol=0)
+
+    run_oracle_trajectory(meta, on_step=check)
+
+
+@pytest.mark.parametrize("name", ["zeeden_f32_c1", "zipsr_f32_c2"])
+def test_oracle_full_size_trajectory_matches_reference(name):
+    """BASELINE configs 1 and 2 at full size (16.8M values, 10 steps)."""
+    if not G.exists(name):
+        pytest.skip("full-size digests not generated")
+    meta, arrays = G.load_traj(name)
+
+    def check(t, inp, params, state):
+        rec = meta["per_step"][t - 1]
+        st = state[0]
+        for key in ("m1_code", "m1_absmax", "m2_code", "m2_absmax"):
+            assert G.sha_np(st[key]) == rec[key], f"{name} step {t} {key}"
+        np.testing.assert_allclose(params[0][::meta["sample_stride"]], arrays[f"s{t}_param_sample"],
+                                   rtol=PARAM_RTOL, atol=PARAM_ATOL)
+
+    run_oracle_trajectory(meta, on_step=check)
