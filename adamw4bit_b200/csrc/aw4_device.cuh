@@ -1,0 +1,265 @@
+// aw4_device.cuh -- device helpers shared by the step and codec kernels.
+//
+// Numerics follow the reference's CPU semantics exactly (nubank/adamw4bit on
+// PyTorch CPU): every float op below is an explicit IEEE round-to-nearest
+// intrinsic so nvcc cannot contract or reassociate, and the library is also
+// compiled with --fmad=false.  The only fused multiply-add is the one torch's
+// lerp uses (m + w * (end - m) as one FMA, adamw.py:557, 684).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/adamw4bit_b200.h"
+
+namespace aw4 {
+
+constexpr int kBlock = AW4_BLOCK;        // values per quantization block
+constexpr int kPerLane = 8;              // consecutive values per thread
+constexpr int kLanesPerBlock = kBlock / kPerLane;  // 16 threads per block
+constexpr int kThreads = 256;            // threads per CTA
+constexpr int kBlocksPerTile = kThreads / kLanesPerBlock;  // 16 blocks = 2048 values
+constexpr float kScaleFloor = 1e-12f;    // quantization.py:706-712 (4-bit schemes)
+
+// ---------------------------------------------------------------------------
+// IEEE float32 ops (no contraction, no reassociation)
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }
+__device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
+__device__ __forceinline__ float fsub(float a, float b) { return __fsub_rn(a, b); }
+__device__ __forceinline__ float fdiv(float a, float b) { return __fdiv_rn(a, b); }
+__device__ __forceinline__ float fsqrt(float a) { return __fsqrt_rn(a); }
+__device__ __forceinline__ float frcp(float a) { return __frcp_rn(a); }
+__device__ __forceinline__ float ffma(float a, float b, float c) { return __fmaf_rn(a, b, c); }
+
+// torch.max / clamp propagate NaN; PTX max.NaN / min.NaN do the same.
+__device__ __forceinline__ float max_nan(float a, float b) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ float min_nan(float a, float b) {
+    float r;
+    asm("min.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ bool is_finite(float a) { return fabsf(a) < __int_as_float(0x7f800000); }
+
+// ---------------------------------------------------------------------------
+// Element IO: 8 consecutive values per thread, 16-byte vector accesses
+// ---------------------------------------------------------------------------
+template <int DT>
+struct Elem;
+
+template <>
+struct Elem<AW4_F32> {
+    static constexpr int kBytes = 4;
+    __device__ __forceinline__ static void load8(const void* base, int64_t e, float v[8]) {
+        const float4* p = reinterpret_cast<const float4*>(static_cast<const float*>(base) + e);
+        float4 a = __ldcs(p), b = __ldcs(p + 1);
+        v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+        v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+    }
+    __device__ __forceinline__ static void store8(void* base, int64_t e, const float v[8]) {
+        float4* p = reinterpret_cast<float4*>(static_cast<float*>(base) + e);
+        __stcs(p, make_float4(v[0], v[1], v[2], v[3]));
+        __stcs(p + 1, make_float4(v[4], v[5], v[6], v[7]));
+    }
+    __device__ __forceinline__ static float round(float v) { return v; }
+    __device__ __forceinline__ static float load1(const void* base, int64_t e) {
+        return static_cast<const float*>(base)[e];
+    }
+    __device__ __forceinline__ static void store1(void* base, int64_t e, float v) {
+        static_cast<float*>(base)[e] = v;
+    }
+};
+
+// bf16: widening is exact; narrowing is round-to-nearest-even like c10::BFloat16.
+__device__ __forceinline__ float bf16_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <>
+struct Elem<AW4_BF16> {
+    static constexpr int kBytes = 2;
+    __device__ __forceinline__ static void load8(const void* base, int64_t e, float v[8]) {
+        uint4 w = __ldcs(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(base) + e));
+        v[0] = bf16_lo(w.x); v[1] = bf16_hi(w.x); v[2] = bf16_lo(w.y); v[3] = bf16_hi(w.y);
+        v[4] = bf16_lo(w.z); v[5] = bf16_hi(w.z); v[6] = bf16_lo(w.w); v[7] = bf16_hi(w.w);
+    }
+    __device__ __forceinline__ static void store8(void* base, int64_t e, const float v[8]) {
+        uint4 w = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
+                             pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+        __stcs(reinterpret_cast<uint4*>(static_cast<uint16_t*>(base) + e), w);
+    }
+    __device__ __forceinline__ static float round(float v) {
+        return __bfloat162float(__float2bfloat16_rn(v));
+    }
+    __device__ __forceinline__ static float load1(const void* base, int64_t e) {
+        return __uint_as_float(((uint32_t) static_cast<const uint16_t*>(base)[e]) << 16);
+    }
+    __device__ __forceinline__ static void store1(void* base, int64_t e, float v) {
+        __nv_bfloat16 h = __float2bfloat16_rn(v);
+        static_cast<uint16_t*>(base)[e] = *reinterpret_cast<uint16_t*>(&h);
+    }
+};
+
+__device__ __forceinline__ float f16_lo(uint32_t w) {
+    return __half2float(__ushort_as_half((unsigned short)(w & 0xffffu)));
+}
+__device__ __forceinline__ float f16_hi(uint32_t w) {
+    return __half2float(__ushort_as_half((unsigned short)(w >> 16)));
+}
+__device__ __forceinline__ uint32_t pack_f16x2(float lo, float hi) {
+    return (uint32_t)__half_as_ushort(__float2half_rn(lo)) |
+           ((uint32_t)__half_as_ushort(__float2half_rn(hi)) << 16);
+}
+
+template <>
+struct Elem<AW4_F16> {
+    static constexpr int kBytes = 2;
+    __device__ __forceinline__ static void load8(const void* base, int64_t e, float v[8]) {
+        uint4 w = __ldcs(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(base) + e));
+        v[0] = f16_lo(w.x); v[1] = f16_hi(w.x); v[2] = f16_lo(w.y); v[3] = f16_hi(w.y);
+        v[4] = f16_lo(w.z); v[5] = f16_hi(w.z); v[6] = f16_lo(w.w); v[7] = f16_hi(w.w);
+    }
+    __device__ __forceinline__ static void store8(void* base, int64_t e, const float v[8]) {
+        uint4 w = make_uint4(pack_f16x2(v[0], v[1]), pack_f16x2(v[2], v[3]),
+                             pack_f16x2(v[4], v[5]), pack_f16x2(v[6], v[7]));
+        __stcs(reinterpret_cast<uint4*>(static_cast<uint16_t*>(base) + e), w);
+    }
+    __device__ __forceinline__ static float round(float v) {
+        return __half2float(__float2half_rn(v));
+    }
+    __device__ __forceinline__ static float load1(const void* base, int64_t e) {
+        return __half2float(__ushort_as_half(static_cast<const uint16_t*>(base)[e]));
+    }
+    __device__ __forceinline__ static void store1(void* base, int64_t e, float v) {
+        static_cast<uint16_t*>(base)[e] = __half_as_ushort(__float2half_rn(v));
+    }
+};
+
+// ---------------------------------------------------------------------------
+// Philox4x32-10 (Salmon, Moraes, Dror, Shaw, SC'11).  Counter layout:
+// (e/4 low word, e/4 high word, step, ordinal); key = 64-bit stream key;
+// element e takes word e%4, top 24 bits -> uniform in [0, 1).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint32_t k0, uint32_t k1) {
+#pragma unroll
+    for (int r = 0; r < 10; ++r) {
+        const uint32_t hi0 = __umulhi(0xD2511F53u, c.x), lo0 = 0xD2511F53u * c.x;
+        const uint32_t hi1 = __umulhi(0xCD9E8D57u, c.z), lo1 = 0xCD9E8D57u * c.z;
+        c = make_uint4(hi1 ^ c.y ^ k0, lo1, hi0 ^ c.w ^ k1, lo0);
+        k0 += 0x9E3779B9u;
+        k1 += 0xBB67AE85u;
+    }
+    return c;
+}
+
+__device__ __forceinline__ float u24(uint32_t r) { return (float)(r >> 8) * 0x1p-24f; }
+
+// 8 uniforms for elements e .. e+7 (e a multiple of 4) of one stream.
+__device__ __forceinline__ void philox_uniform8(uint64_t key, uint32_t step, uint32_t ordinal,
+                                                uint64_t e, float u[8]) {
+    const uint64_t q = e >> 2;
+    const uint32_t k0 = (uint32_t)key, k1 = (uint32_t)(key >> 32);
+    uint4 r0 = philox4x32_10(make_uint4((uint32_t)q, (uint32_t)(q >> 32), step, ordinal), k0, k1);
+    uint4 r1 = philox4x32_10(
+        make_uint4((uint32_t)(q + 1), (uint32_t)((q + 1) >> 32), step, ordinal), k0, k1);
+    u[0] = u24(r0.x); u[1] = u24(r0.y); u[2] = u24(r0.z); u[3] = u24(r0.w);
+    u[4] = u24(r1.x); u[5] = u24(r1.y); u[6] = u24(r1.z); u[7] = u24(r1.w);
+}
+
+// ---------------------------------------------------------------------------
+// Rounding search (built by aw4_scheme_prepare)
+// ---------------------------------------------------------------------------
+struct SmemScheme {
+    uint8_t lut[AW4_LUT_BINS];
+    float2 thr2[17];      // (thr[k], thr[k+1])
+    float cb[16];
+    float pad[2];
+};
+
+__device__ __forceinline__ void load_scheme(SmemScheme& s, const aw4_scheme& g, int tid,
+                                            int nthreads) {
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(g.lut);
+    uint32_t* dst = reinterpret_cast<uint32_t*>(s.lut);
+    for (int i = tid; i < AW4_LUT_BINS / 4; i += nthreads) dst[i] = src[i];
+    for (int i = tid; i < 17; i += nthreads) s.thr2[i] = make_float2(g.thr[i], g.thr[i + 1]);
+    for (int i = tid; i < 16; i += nthreads) s.cb[i] = g.codebook[i];
+}
+
+// For RTN schemes: the stored code of normalised value x (finite, |x| <= 1).
+// For SR schemes: the searchsorted-left index i in [0, 16].
+__device__ __forceinline__ int lut_search(const SmemScheme& s, float x) {
+    int b = __float2int_rz(ffma(x, 1024.0f, 1024.0f));
+    b = min(max(b, 0), AW4_LUT_BINS - 1);
+    const int k = s.lut[b];
+    const float2 t = s.thr2[k];
+    return k + (x >= t.y ? 1 : 0) - (x < t.x ? 1 : 0);
+}
+
+// torch.searchsorted(cb, x) (left): the ATen lower-bound loop, NaN -> 16.
+__device__ __forceinline__ int searchsorted_left(const float* cb, float x) {
+    int start = 0, end = 16;
+    while (start < end) {
+        const int mid = start + ((end - start) >> 1);
+        if (!(cb[mid] >= x)) start = mid + 1; else end = mid;
+    }
+    return start;
+}
+
+// Literal RTN rule of quantization.py:263-272 (used for non-finite blocks).
+__device__ __forceinline__ int rtn_literal(const float* cb, float x) {
+    const int i = searchsorted_left(cb, x);
+    const int l = max(i - 1, 0), r = min(i, 15);
+    return (fabsf(fsub(x, cb[l])) < fabsf(fsub(cb[r], x))) ? l : r;
+}
+
+// Value-unbiased SR given the interval index (quantization.py:295-315).
+__device__ __forceinline__ int value_sr_from_index(const float* cb, int i, float x, float u) {
+    const int l = max(i - 1, 0), r = min(i, 15);
+    const float a = cb[l], b = cb[r];
+    const float width = fsub(b, a);
+    float p = fdiv(fsub(x, a), max_nan(width, 1e-12f));
+    p = (width > 0.0f) ? p : 0.0f;
+    p = min_nan(max_nan(p, 0.0f), 1.0f);
+    return (u < p) ? r : l;
+}
+
+// Adam preconditioner 1 / (sqrt(max(s * l / bias, 0)) + eps) (quantization.py:356-358).
+__device__ __forceinline__ float precond(float s, float level, float bias, float eps) {
+    return frcp(fadd(fsqrt(max_nan(fdiv(fmul(s, level), bias), 0.0f)), eps));
+}
+
+// Preconditioner-space SR given the interval index and the block's level
+// preconditioners f[k] = precond(s, cb[k]) (quantization.py:336-377).
+__device__ __forceinline__ int update_sr_from_index(const float* cb, const float* f, int i,
+                                                    float x, float s, float bias, float eps,
+                                                    float u) {
+    const int l = max(i - 1, 0), r = min(i, 15);
+    const float width = fsub(cb[r], cb[l]);
+    const float fl = f[l], fr = f[r];
+    const float fx = precond(s, x, bias, eps);
+    const float den = fsub(fl, fr);
+    float p = fdiv(fsub(fx, fr), max_nan(den, 1e-30f));
+    p = (width > 0.0f && den > 0.0f) ? p : 1.0f;
+    p = min_nan(max_nan(p, 0.0f), 1.0f);
+    return (u < p) ? l : r;
+}
+
+// Max over the 16 lanes of a block group (lanes 16h .. 16h+15 of a warp).
+__device__ __forceinline__ float group_max16(float v) {
+    v = max_nan(v, __shfl_xor_sync(0xffffffffu, v, 8));
+    v = max_nan(v, __shfl_xor_sync(0xffffffffu, v, 4));
+    v = max_nan(v, __shfl_xor_sync(0xffffffffu, v, 2));
+    v = max_nan(v, __shfl_xor_sync(0xffffffffu, v, 1));
+    return v;
+}
+
+}  // namespace aw4

@@ -1,0 +1,134 @@
+// aw4_encode.cuh -- block encoder shared by the fused step and the codec.
+//
+// A 128-value block is held by a group of 16 consecutive lanes, 8 values
+// each (lane j holds values 8j .. 8j+7).  The encoder reproduces
+// quantization.py:_quantize_impl (lines 937-960) for 4-bit codebooks:
+//   scale = max(absmax(block), 1e-12); x = v / scale; codes by RTN or SR;
+//   optional zero floor (dyn4_nz); optional EDEN scale calibration.
+#pragma once
+
+#include "aw4_device.cuh"
+
+namespace aw4 {
+
+// Per-warp scratch for EDEN sums and the update-SR level table.
+// EDEN: four 136-float tables (num/den x 2 groups); the 8-float pad between
+// tables puts the 32 lanes' column reads on 32 distinct banks.
+constexpr int kEdenTable = 136;
+constexpr int kWarpScratch = 4 * kEdenTable + 32 /* column totals */ + 32 /* level table */;
+
+struct GroupCtx {
+    float* eden_num;   // this group's 128-float products table
+    float* eden_den;
+    float* totals;     // 16 floats: 8 num column totals, 8 den column totals
+    float* levels;     // 16 floats: update-SR preconditioner of each level
+    int j;             // lane within the group (0..15)
+};
+
+__device__ __forceinline__ GroupCtx group_ctx(float* warp_scratch, int lane) {
+    const int h = lane >> 4;
+    GroupCtx g;
+    g.eden_num = warp_scratch + (2 * h) * kEdenTable;
+    g.eden_den = warp_scratch + (2 * h + 1) * kEdenTable;
+    g.totals = warp_scratch + 4 * kEdenTable + 16 * h;
+    g.levels = warp_scratch + 4 * kEdenTable + 32 + 16 * h;
+    g.j = lane & 15;
+    return g;
+}
+
+// Sum of the block's 128 products in torch's CPU reduction order for
+// (nb, 128).sum(dim=1): vector v (values 8v .. 8v+7) accumulates into
+// accumulator v % 4, the accumulators combine in order, then the 8 lanes are
+// summed in order from zero.  Lane j of the group holds vector v = j.
+// Returns (num, den) totals, valid in every lane of the group.
+__device__ __forceinline__ float2 eden_sums(const GroupCtx& g, const float np[8],
+                                            const float dp[8]) {
+    float4* rn = reinterpret_cast<float4*>(g.eden_num + 8 * g.j);
+    float4* rd = reinterpret_cast<float4*>(g.eden_den + 8 * g.j);
+    rn[0] = make_float4(np[0], np[1], np[2], np[3]);
+    rn[1] = make_float4(np[4], np[5], np[6], np[7]);
+    rd[0] = make_float4(dp[0], dp[1], dp[2], dp[3]);
+    rd[1] = make_float4(dp[4], dp[5], dp[6], dp[7]);
+    __syncwarp();
+    // lanes 0-7: numerator column c; lanes 8-15: denominator column c
+    const float* tab = (g.j < 8) ? g.eden_num : g.eden_den;
+    const int c = g.j & 7;
+    float acc[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        float a = fadd(0.0f, tab[8 * k + c]);
+        a = fadd(a, tab[8 * (k + 4) + c]);
+        a = fadd(a, tab[8 * (k + 8) + c]);
+        a = fadd(a, tab[8 * (k + 12) + c]);
+        acc[k] = a;
+    }
+    g.totals[g.j] = fadd(fadd(fadd(acc[0], acc[1]), acc[2]), acc[3]);
+    __syncwarp();
+    const float4* tn = reinterpret_cast<const float4*>(g.totals);
+    const float4 n0 = tn[0], n1 = tn[1], d0 = tn[2], d1 = tn[3];
+    float num = fadd(0.0f, n0.x);
+    num = fadd(num, n0.y); num = fadd(num, n0.z); num = fadd(num, n0.w);
+    num = fadd(num, n1.x); num = fadd(num, n1.y); num = fadd(num, n1.z); num = fadd(num, n1.w);
+    float den = fadd(0.0f, d0.x);
+    den = fadd(den, d0.y); den = fadd(den, d0.z); den = fadd(den, d0.w);
+    den = fadd(den, d1.x); den = fadd(den, d1.y); den = fadd(den, d1.z); den = fadd(den, d1.w);
+    __syncwarp();  // scratch is reused by the next block
+    return make_float2(num, den);
+}
+
+// Encodes the group's block.  v: this lane's 8 working values.  u: 8 uniforms
+// (SR modes).  Returns this lane's 8 codes packed as nibbles (value 8j+i in
+// bits 4i..4i+3, i.e. the reference's little-endian nibble order) and sets
+// *scale_out to the block scale to store (identical in all 16 lanes).
+template <int MODE>
+__device__ __forceinline__ uint32_t encode_block(const SmemScheme& S, const GroupCtx& g,
+                                                 const float v[8], const float u[8],
+                                                 int zero_floor, int eden, float sr_bias,
+                                                 float sr_eps, float* scale_out) {
+    float amax = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = max_nan(amax, fabsf(v[i]));
+    amax = group_max16(amax);
+    const float sc = max_nan(amax, kScaleFloor);
+    const bool fin = is_finite(sc);
+    if (MODE == AW4_SR_UPDATE) {
+        g.levels[g.j] = precond(sc, S.cb[g.j], sr_bias, sr_eps);
+        __syncwarp();
+    }
+    float x[8];
+    int code[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        x[i] = fdiv(v[i], sc);
+        if (MODE == AW4_RTN) {
+            code[i] = fin ? lut_search(S, x[i]) : rtn_literal(S.cb, x[i]);
+        } else {
+            const int idx = fin ? lut_search(S, x[i]) : searchsorted_left(S.cb, x[i]);
+            if (MODE == AW4_SR_VALUE)
+                code[i] = value_sr_from_index(S.cb, idx, x[i], u[i]);
+            else
+                code[i] = update_sr_from_index(S.cb, g.levels, idx, x[i], sc, sr_bias, sr_eps,
+                                               u[i]);
+        }
+        if (zero_floor) code[i] = max(code[i], 1);
+    }
+    if (MODE == AW4_SR_UPDATE) __syncwarp();  // level table reused by the next block
+    float s = sc;
+    if (eden) {
+        float np[8], dp[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            np[i] = fmul(x[i], x[i]);
+            dp[i] = fmul(x[i], S.cb[code[i]]);
+        }
+        const float2 nd = eden_sums(g, np, dp);
+        s = fmul(sc, fdiv(nd.x, max_nan(nd.y, kScaleFloor)));
+    }
+    *scale_out = s;
+    uint32_t packed = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) packed |= (uint32_t)code[i] << (4 * i);
+    return packed;
+}
+
+}  // namespace aw4

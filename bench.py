@@ -1,0 +1,364 @@
+"""Benchmark of the fused 4-bit AdamW step.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...          (N > 1)
+
+Workload: the Llama-3-8B parameter set (vocab 128256, d 4096, 32 layers, ffn
+14336, 32/8 heads, untied head: 291 tensors, 8.03 B values, all quantized),
+FP32 master parameters, BF16 gradients N(0, 1e-4), ZEEDENAdamW4Bit (NF4 m1 +
+zero-exclusive Dyn4 m2 with EDEN).  N=1 steps the whole set through the public
+optimizer API; N>1 shards it ZeRO-1 style (ZeRO1AdamW4Bit) and all-gathers the
+updated FP32 parameters with NCCL.  Synthetic data, random-init weights.
+
+A step is one pass of the optimizer over every parameter.  ``value`` is the
+whole-job elements/s with everything resident in HBM (the 56 GB working set
+is far larger than L2, so no flush is needed between steps); ``e2e`` is the
+same metric through the public API with the gradients copied in from pinned
+host memory and the updated parameters copied back each step.
+``--impl reference`` times the CPU oracle port of the reference algorithm on
+the host's cores on a bounded sample of the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "optimizer-step elements/s"
+UNIT = "elements/s"
+B_PER_ELEM = 4 + 4 + 2 + 1 + 1 + 2 * 8 / 128   # FP32 p r+w, BF16 g r, codes r+w, scales r+w
+WORKLOAD = "llama3-8b ZE-EDEN fp32-master/bf16-grad (BASELINE config 5)"
+
+
+def llama3_8b_shapes() -> list[tuple[int, ...]]:
+    V, d, L, ffn, kv = 128256, 4096, 32, 14336, 1024
+    shapes = [(V, d)]
+    for _ in range(L):
+        shapes += [(d, d), (kv, d), (kv, d), (d, d), (ffn, d), (ffn, d), (d, ffn), (d,), (d,)]
+    shapes += [(d,), (V, d)]
+    return shapes
+
+
+def measured_peaks() -> dict:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except OSError:
+        return {}
+
+
+def traffic_record() -> dict | None:
+    try:
+        with open(os.path.join(ROOT, "profiles", "ncu_traffic.json")) as f:
+            return json.load(f)
+    except OSError:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.idx = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100", "-i", str(self.idx)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        out, _ = self.proc.communicate(timeout=10)
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(n_gpus: int):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}")
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def make_workload(dev, shapes, seed=0):
+    g = torch.Generator(device=dev).manual_seed(seed)
+    params, grads = [], []
+    for s in shapes:
+        p = torch.nn.Parameter(torch.randn(s, device=dev, generator=g) * 0.02)
+        gr = (torch.randn(s, device=dev, generator=g) * 1e-4).to(torch.bfloat16)
+        p.grad_dtype = None  # FP32 parameter, BF16 gradient
+        params.append(p)
+        grads.append(gr)
+    return params, grads
+
+
+def cpu_oracle_rate(sample_elems: int, steps: int, threads: int | None = None) -> dict:
+    """Time the oracle port of the reference algorithm on the host cores."""
+    import numpy as np
+
+    from oracle import oracle as O
+    if threads:
+        O.set_threads(threads)
+    n = sample_elems
+    rng = np.random.default_rng(0)
+    p = (rng.standard_normal(n, dtype=np.float32) * 0.02).astype(np.float32)
+    g32 = (rng.standard_normal(n, dtype=np.float32) * 1e-4).astype(np.float32)
+    g = (g32.view(np.uint32) >> 16).astype(np.uint16)   # bf16 (truncated; values only)
+    c1, s1 = O.init_zero("nf4", n)
+    c2, s2 = O.init_zero("dyn4_nz", n, eden=True)
+    times = []
+    for t in range(1, steps + 2):
+        cfg = O.make_cfg(m1_scheme="nf4", m2_scheme="dyn4_nz", eden=True, lr=1e-3,
+                         betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, step=t,
+                         grad_dtype=O.BF16)
+        t0 = time.perf_counter()
+        O.step(cfg, p, g, c1, s1, c2, s2)
+        dt = time.perf_counter() - t0
+        if t > 1:
+            times.append(dt)
+    med = statistics.median(times)
+    return {"value": n / med, "unit": UNIT, "cores": O.max_threads(), "kind": "port",
+            "sample": f"{n} values (FP32 params, BF16 grads, ZE-EDEN), median of {steps} steps "
+                      f"after 1 warm-up step, C oracle (OpenMP)",
+            "seconds_per_step": med}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    from oracle import oracle as O
+    threads = os.cpu_count() or 1
+    O.set_threads(threads)
+    sample = args.cpu_sample
+    base = cpu_oracle_rate(sample, max(1, args.steps), threads)
+    line = {"metric": METRIC, "value": base["value"], "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": base["seconds_per_step"] * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "sample_values": sample, "l2": "inputs > L2"},
+            "impl": "reference",
+            "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args, rank, world, local):
+    from adamw4bit_b200 import ZEEDENAdamW4Bit, _native
+    from adamw4bit_b200.zero import ZeRO1AdamW4Bit
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    shapes = llama3_8b_shapes()
+    if args.layers is not None:
+        shapes = shapes[:1 + 9 * args.layers] + shapes[-2:]
+    total = sum(int(torch.Size(s).numel()) for s in shapes)
+    params, grads = make_workload(dev, shapes)
+    if world == 1:
+        opt = ZEEDENAdamW4Bit(params, lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+        step_fn = opt.step
+        updated_per_rank = total
+    else:
+        opt = ZeRO1AdamW4Bit(params, recipe="ze-eden", rounds=args.rounds)
+        step_fn = opt.step
+        updated_per_rank = opt.owned_numel()
+    for p, g in zip(params, grads):
+        p.grad = g
+    for _ in range(args.warmup):
+        step_fn()
+    barrier(world)
+
+    sampler = ClockSampler(torch.cuda.current_device() if world == 1 else local)
+    if rank == 0 or world > 1:
+        sampler.start()
+    opt.launch_timings = []
+    launches0 = _native.launch_count()
+    barrier(world)
+    cur = torch.cuda.current_stream(dev)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(cur)
+    for _ in range(args.steps):
+        step_fn()
+    e1.record(cur)
+    barrier(world)
+    launches = _native.launch_count() - launches0
+    clocks = sampler.stop()
+    elapsed_ms = e0.elapsed_time(e1)
+    timings = opt.launch_timings
+    opt.launch_timings = None
+    kernel_ms = sum(a.elapsed_time(b) for a, b, *_ in timings)
+    kernel_elems = sum(n for _, _, n, *_ in timings)
+    elapsed_ms = max_over_ranks(elapsed_ms, world)
+    kernel_ms_max = max_over_ranks(kernel_ms, world)
+    ms_per_step = elapsed_ms / args.steps
+    value = total * args.steps / (elapsed_ms / 1e3)
+
+    peaks = measured_peaks()
+    hbm_peak = peaks.get("hbm_gbs")
+    peak_src = "measured"
+    if hbm_peak is None:
+        hbm_peak, peak_src = 6650.0, "fallback"
+    per_launch_ms = kernel_ms / max(1, len(timings))
+    per_launch_elems = kernel_elems / max(1, len(timings))
+    achieved = per_launch_elems * B_PER_ELEM / (per_launch_ms / 1e3) / 1e9
+    tr = traffic_record()
+    traffic = None
+    if tr and tr.get("bytes_per_value"):
+        traffic = tr["bytes_per_value"] * per_launch_elems
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
+                "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
+                "peak_source": peak_src,
+                "algorithmic_bytes_per_value": B_PER_ELEM,
+                "kernel": "aw4::step_kernel<F32,BF16,RTN,RTN> (fused decode+AdamW+encode)",
+                "launch_ms": round(per_launch_ms, 4), "values_per_launch": int(per_launch_elems)}
+
+    e2e = run_e2e(args, opt, params, grads, dev, world, total) if args.e2e_steps > 0 else None
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+                "dtype": "f32", "data": "synthetic",
+                "config": {"workload": WORKLOAD, "values": total, "tensors": len(shapes),
+                           "param_dtype": "fp32", "grad_dtype": "bf16", "recipe": "ZE-EDEN",
+                           "parallelism": "single GPU" if world == 1 else f"zero1-dp{world}",
+                           "l2": "no flush: 56 GB working set >> 126 MB L2"},
+                "roofline": roofline,
+                "update_only": {"values_per_rank": updated_per_rank,
+                                "kernel_ms_per_step_max_rank": kernel_ms_max / args.steps,
+                                "elements_per_s_per_rank":
+                                    updated_per_rank * args.steps / (kernel_ms_max / 1e3)},
+                "clocks": clocks, "gpu_launches": int(launches),
+                "e2e": e2e}
+        if world == 1 and args.cpu_sample > 0:
+            line["cpu_baseline"] = {k: v for k, v in cpu_oracle_rate(
+                args.cpu_sample, args.cpu_steps).items() if k != "seconds_per_step"}
+        print(json.dumps(line), flush=True)
+
+
+def run_e2e(args, opt, params, grads, dev, world, total):
+    """Public-API step with host buffers: pinned grads -> device, step,
+    updated params -> pinned host, all inside the timed region."""
+    host_g = [g.detach().to("cpu").pin_memory() for g in grads]
+    host_p = [torch.empty(p.shape, dtype=p.dtype, pin_memory=True) for p in params]
+    h2d = sum(g.numel() * g.element_size() for g in host_g)
+    d2h = sum(p.numel() * p.element_size() for p in host_p)
+    cur = torch.cuda.current_stream(dev)
+
+    def one():
+        for p, hg in zip(params, host_g):
+            p.grad.copy_(hg, non_blocking=True)
+        opt.step()
+        for p, hp in zip(params, host_p):
+            hp.copy_(p.detach(), non_blocking=True)
+
+    one()
+    barrier(world)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(cur)
+    for _ in range(args.e2e_steps):
+        one()
+    e1.record(cur)
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    del host_g, host_p
+    return {"value": total * args.e2e_steps / (ms / 1e3), "unit": UNIT,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "ms_per_step": ms / args.e2e_steps, "steps": args.e2e_steps}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--rounds", type=int, default=4, help="ZeRO-1 gather rounds")
+    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--cpu-sample", type=int, default=1 << 27,
+                    help="values in the CPU-oracle sample (0: skip)")
+    ap.add_argument("--cpu-steps", type=int, default=3)
+    ap.add_argument("--layers", type=int, default=None, help="debug: fewer decoder layers")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, rank, int(os.environ.get("WORLD_SIZE", "1")))
+        return
+    rank, world, local = dist_setup(args.gpus)
+    try:
+        run_ours(args, rank, world, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
