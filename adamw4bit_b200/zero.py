@@ -39,6 +39,51 @@ _M2_OFFSET = 0x5E6F7789
 _MAX_SEED = (1 << 63) - 1
 
 
+class ShardPlan:
+    """Block-cyclic ownership of a flat index space of tensors (pure host logic).
+
+    ``chunk`` (c) is a multiple of 128; round i covers [i*W*c, (i+1)*W*c) and
+    rank r owns [i*W*c + r*c, i*W*c + (r+1)*c) clipped to the real data.  For
+    each round a rank's segments are (tensor index, start within the tensor,
+    length, offset within the rank's state buffers)."""
+
+    def __init__(self, sizes: list[int], world: int, rank: int, rounds: int):
+        if any(n % 128 for n in sizes):
+            raise ValueError("tensor sizes must be multiples of 128")
+        self.sizes = list(sizes)
+        self.world, self.rank = world, rank
+        self.rounds = max(1, int(rounds))
+        self.total = sum(sizes)
+        c = math.ceil(self.total / (world * self.rounds) / 128) * 128
+        self.chunk = max(c, 128)
+        self.padded = self.chunk * world * self.rounds
+        self.starts = []
+        off = 0
+        for n in sizes:
+            self.starts.append(off)
+            off += n
+        self.owned = []
+        for i in range(self.rounds):
+            a = i * world * self.chunk + rank * self.chunk
+            self.owned.append((a, max(a, min(a + self.chunk, self.total))))
+        self.segments = []
+        state_off = 0
+        for a, b in self.owned:
+            segs = []
+            for ti, (n, s0) in enumerate(zip(self.sizes, self.starts)):
+                lo, hi = max(a, s0), min(b, s0 + n)
+                if lo < hi:
+                    segs.append((ti, lo - s0, hi - lo, state_off + (lo - a)))
+            self.segments.append(segs)
+            state_off += self.chunk
+
+    def owned_numel(self) -> int:
+        return sum(b - a for a, b in self.owned)
+
+    def state_numel(self) -> int:
+        return self.chunk * self.rounds
+
+
 class ZeRO1AdamW4Bit:
     """Sharded fused step over quantized parameters (every tensor eligible:
     numel a multiple of 128 and at least 4096).
@@ -74,32 +119,20 @@ class ZeRO1AdamW4Bit:
         self.device, self.dtype = dev, dtype
         self.keys = ((quant_rng_seed + _M1_OFFSET) % _MAX_SEED,
                      (quant_rng_seed + _M2_OFFSET) % _MAX_SEED)
-        total = sum(p.numel() for p in self.params)
         W = self.world
-        self.rounds = max(1, int(rounds))
-        c = math.ceil(total / (W * self.rounds) / 128) * 128
-        self.chunk = c
-        self.padded = c * W * self.rounds
-        self.total = total
+        plan = ShardPlan([p.numel() for p in self.params], W, self.rank, rounds)
+        self.plan = plan
+        self.chunk, self.padded, self.total = plan.chunk, plan.padded, plan.total
         # re-home parameters into one flat buffer (zero padding at the end)
-        flat = torch.zeros(self.padded, dtype=dtype, device=dev)
-        starts, off = [], 0
-        for p in self.params:
+        flat = torch.zeros(plan.padded, dtype=dtype, device=dev)
+        for p, off in zip(self.params, plan.starts):
             n = p.numel()
             flat[off:off + n].copy_(p.detach().reshape(-1))
             p.data = flat[off:off + n].view(p.shape)
-            starts.append(off)
-            off += n
         self.flat = flat
-        self.starts = starts
-        # owned ranges: round i -> [i*W*c + r*c, i*W*c + (r+1)*c) clipped to the real data
-        owned = []
-        for i in range(self.rounds):
-            a = i * W * c + self.rank * c
-            owned.append((a, min(a + c, total)))
-        self.owned = owned
+        self.owned = plan.owned
         # state for the owned elements, one flat buffer per kind
-        n_own = c * self.rounds
+        n_own = plan.state_numel()
         self.m1_codes = torch.empty(n_own // 2, dtype=torch.uint8, device=dev)
         self.m2_codes = torch.empty(n_own // 2, dtype=torch.uint8, device=dev)
         self.m1_scales = torch.empty(n_own // 128, dtype=torch.float32, device=dev)
@@ -111,25 +144,9 @@ class ZeRO1AdamW4Bit:
                                                 N.ptr(scales), n_own, dev.index, stream),
                     "aw4_init_zero_state")
         self.step_count = 0
-        self.segments = self._segments()
+        self.segments = plan.segments
         self.gather_stream = torch.cuda.Stream(dev) if W > 1 else None
         self.launch_timings: list | None = None
-
-    def _segments(self):
-        """Per round: (tensor index, start in tensor, length, offset in state)."""
-        out = []
-        state_off = 0
-        for r, (a, b) in enumerate(self.owned):
-            segs = []
-            pos = a
-            for ti, (p, s0) in enumerate(zip(self.params, self.starts)):
-                s1 = s0 + p.numel()
-                lo, hi = max(pos, s0), min(b, s1)
-                if lo < hi:
-                    segs.append((ti, lo - s0, hi - lo, state_off + (lo - a)))
-            out.append(segs)
-            state_off += self.chunk
-        return out
 
     @torch.no_grad()
     def step(self) -> None:
@@ -182,4 +199,4 @@ class ZeRO1AdamW4Bit:
             cur.wait_stream(self.gather_stream)
 
     def owned_numel(self) -> int:
-        return sum(b - a for a, b in self.owned if b > a)
+        return self.plan.owned_numel()
