@@ -20,7 +20,7 @@ AW4_OK, AW4_ERR_INVALID, AW4_ERR_CUDA, AW4_ERR_UNSUPPORTED = 0, 1, 2, 3
 F32, BF16, F16 = 0, 1, 2
 RTN, SR_VALUE, SR_UPDATE = 0, 1, 2
 BLOCK = 128
-LUT_BINS = 2048
+LUT_BINS = 1024
 ABI_VERSION = 1
 
 DTYPE_CODES = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}

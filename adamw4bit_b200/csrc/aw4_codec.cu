@@ -26,7 +26,7 @@ __global__ void __launch_bounds__(kThreads)
 quantize_kernel(const __grid_constant__ aw4_scheme scheme, int eden, const float* x,
                 int64_t n_blocks, uint8_t* codes, float* scales, const float* draws,
                 uint64_t key, uint32_t step, uint32_t ordinal, float sr_bias, float sr_eps) {
-    __shared__ __align__(16) SmemScheme S;
+    __shared__ __align__(16) SmemSchemeT<true> S;
     __shared__ __align__(16) float scratch[kThreads / 32][kWarpScratch];
     load_scheme(S, scheme, threadIdx.x, kThreads);
     __syncthreads();
@@ -52,7 +52,8 @@ quantize_kernel(const __grid_constant__ aw4_scheme scheme, int eden, const float
             }
         }
         float s;
-        const uint32_t c = encode_block<MODE>(S, g, v, u, scheme.zero_floor, eden, sr_bias, sr_eps, &s);
+        const uint32_t c = encode_block<MODE>(S, g, v, lane_absmax(v), u, scheme.zero_floor, eden,
+                                              sr_bias, sr_eps, &s);
         if (active) {
             reinterpret_cast<uint32_t*>(codes)[e0 >> 3] = c;
             if (g.j == 0) scales[blk] = s;

@@ -12,6 +12,9 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstddef>
+#include <type_traits>
+
 #include "../../include/adamw4bit_b200.h"
 
 namespace aw4 {
@@ -46,6 +49,87 @@ __device__ __forceinline__ float min_nan(float a, float b) {
     return r;
 }
 __device__ __forceinline__ bool is_finite(float a) { return fabsf(a) < __int_as_float(0x7f800000); }
+
+// Correctly rounded a / b from y = RN(1 / b) (Markstein, "Computation of
+// elementary functions on the IBM RISC System/6000 processor", IBM J. Res.
+// Dev. 34(1), 1990): q = RN(a*y) is within one ulp, the remainder
+// r = a - q*b is exact in one FMA, and RN(q + r*y) is RN(a/b).  Preconditions
+// (checked by the callers): b and y normal, and a == 0 or |a| >= 2^-100, so
+// the quotient is normal and the remainder cannot underflow.
+__device__ __forceinline__ float div_markstein(float a, float b, float y) {
+    const float q = fmul(a, y);
+    const float r = ffma(-q, b, a);
+    return ffma(r, y, q);
+}
+constexpr float kMarksteinMinNumerator = 0x1p-100f;
+constexpr float kMarksteinMaxDivisor = 0x1p26f;
+constexpr float kMarksteinMinDivisor = 0x1p-100f;
+
+// True if some value is a nonzero of magnitude below 2^-100 (it takes the
+// IEEE division path instead of div_markstein).
+__device__ __forceinline__ bool any_tiny(const float v[8]) {
+    bool t = false;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) t |= (fabsf(v[i]) < kMarksteinMinNumerator) & (v[i] != 0.0f);
+    return t;
+}
+
+// Packed float32 pairs (Blackwell f32x2, IEEE round-to-nearest).  Only FMA
+// and multiply are provided: ptxas may contract a packed multiply feeding a
+// packed add/sub into one FMA (even with explicit .rn), which would break
+// bit-exactness, so additions stay scalar and packed products must feed only
+// FMA operands, divisions or memory.
+__device__ __forceinline__ unsigned long long pk2(float lo, float hi) {
+    unsigned long long r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ void upk2(unsigned long long r, float& lo, float& hi) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+}
+// d[i] = a[i] * b[i] for i in 0..7
+__device__ __forceinline__ void vmul8(float d[8], const float a[8], const float b[8]) {
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+        unsigned long long r;
+        asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(pk2(a[i], a[i + 1])), "l"(pk2(b[i], b[i + 1])));
+        upk2(r, d[i], d[i + 1]);
+    }
+}
+// d[i] = a[i] * s
+__device__ __forceinline__ void vmuls8(float d[8], const float a[8], float s) {
+    const unsigned long long ss = pk2(s, s);
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+        unsigned long long r;
+        asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(pk2(a[i], a[i + 1])), "l"(ss));
+        upk2(r, d[i], d[i + 1]);
+    }
+}
+// d[i] = fma(s, a[i], c[i])
+__device__ __forceinline__ void vfmas8(float d[8], float s, const float a[8], const float c[8]) {
+    const unsigned long long ss = pk2(s, s);
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+        unsigned long long r;
+        asm("fma.rn.f32x2 %0, %1, %2, %3;"
+            : "=l"(r) : "l"(ss), "l"(pk2(a[i], a[i + 1])), "l"(pk2(c[i], c[i + 1])));
+        upk2(r, d[i], d[i + 1]);
+    }
+}
+// q[i] = RN(a[i] / b) with y = RN(1 / b) (div_markstein, pairwise)
+__device__ __forceinline__ void vdiv_markstein8(float q[8], const float a[8], float b, float y) {
+    const unsigned long long bb = pk2(-b, -b), yy = pk2(y, y);
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+        const unsigned long long aa = pk2(a[i], a[i + 1]);
+        unsigned long long q0, r, q1;
+        asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(q0) : "l"(aa), "l"(yy));
+        asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(q0), "l"(bb), "l"(aa));
+        asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(q1) : "l"(r), "l"(yy), "l"(q0));
+        upk2(q1, q[i], q[i + 1]);
+    }
+}
 
 // ---------------------------------------------------------------------------
 // Element IO: 8 consecutive values per thread, 16-byte vector accesses
@@ -176,32 +260,100 @@ __device__ __forceinline__ void philox_uniform8(uint64_t key, uint32_t step, uin
 }
 
 // ---------------------------------------------------------------------------
-// Rounding search (built by aw4_scheme_prepare)
+// Rounding search (tables built by aw4_scheme_prepare)
 // ---------------------------------------------------------------------------
-struct SmemScheme {
-    uint8_t lut[AW4_LUT_BINS];
-    float2 thr2[17];      // (thr[k], thr[k+1])
-    float cb[16];
-    float pad[2];
+// Rounding-search entry for bin edge b (x = -1 + b/512): the next threshold
+// above the edge and the code at the edge; the EDEN flavour also carries the
+// levels of that code and the next one.  For RTN schemes with the dyn4_nz
+// floor the floor is folded in: codes below 1 read as 1.
+struct __align__(8) SearchEntry {
+    float next_thr;
+    int code;
+};
+struct __align__(16) SearchEntryL {
+    float next_thr;
+    int code;
+    float level;
+    float level_next;
 };
 
-__device__ __forceinline__ void load_scheme(SmemScheme& s, const aw4_scheme& g, int tid,
-                                            int nthreads) {
-    const uint32_t* src = reinterpret_cast<const uint32_t*>(g.lut);
-    uint32_t* dst = reinterpret_cast<uint32_t*>(s.lut);
-    for (int i = tid; i < AW4_LUT_BINS / 4; i += nthreads) dst[i] = src[i];
-    for (int i = tid; i < 17; i += nthreads) s.thr2[i] = make_float2(g.thr[i], g.thr[i + 1]);
+template <bool LEVELS>
+struct __align__(16) SmemSchemeT {
+    typename std::conditional<LEVELS, SearchEntryL, SearchEntry>::type tab[AW4_LUT_BINS + 1];
+    float cb[16];
+    float2 pair[256];  // packed code byte -> (cb[low nibble], cb[high nibble])
+};
+// lut_search reads entries as float2 / float4 and decode8 reads pairs as float2
+static_assert(alignof(SmemSchemeT<true>) == 16 && alignof(SmemSchemeT<false>) == 16, "");
+static_assert(sizeof(SearchEntryL) == 16 && sizeof(SearchEntry) == 8, "");
+static_assert(offsetof(SmemSchemeT<true>, pair) % 8 == 0, "");
+static_assert(offsetof(SmemSchemeT<false>, pair) % 8 == 0, "");
+
+template <bool LEVELS>
+__device__ __forceinline__ void load_scheme(SmemSchemeT<LEVELS>& s, const aw4_scheme& g,
+                                            int tid, int nthreads) {
+    const bool floor_in_table = g.zero_floor && g.round_mode == AW4_RTN;
+    for (int b = tid; b <= AW4_LUT_BINS; b += nthreads) {
+        int k;
+        if (b < AW4_LUT_BINS) {
+            k = g.lut[b];
+        } else {  // edge x = 1.0: one more threshold may sit in the last bin
+            k = g.lut[AW4_LUT_BINS - 1];
+            k += (g.thr[k + 1] <= 1.0f) ? 1 : 0;
+        }
+        float next = g.thr[k + 1];
+        if (floor_in_table && k == 0) {
+            // code(x) = max(0 + (x >= t1), 1) = 1 on this whole bin: the only
+            // threshold a bin can hold is t1, which moves no floored code
+            k = 1;
+            next = (g.thr[2] >= -1.0f + (float)(b + 1) / 512.0f) ? INFINITY : g.thr[2];
+        }
+        if constexpr (LEVELS) {
+            s.tab[b] = SearchEntryL{next, k, g.codebook[min(k, 15)], g.codebook[min(k + 1, 15)]};
+        } else {
+            s.tab[b] = SearchEntry{next, k};
+        }
+    }
     for (int i = tid; i < 16; i += nthreads) s.cb[i] = g.codebook[i];
+    for (int i = tid; i < 256; i += nthreads)
+        s.pair[i] = make_float2(g.codebook[i & 15], g.codebook[i >> 4]);
 }
 
-// For RTN schemes: the stored code of normalised value x (finite, |x| <= 1).
-// For SR schemes: the searchsorted-left index i in [0, 16].
-__device__ __forceinline__ int lut_search(const SmemScheme& s, float x) {
-    int b = __float2int_rz(ffma(x, 1024.0f, 1024.0f));
-    b = min(max(b, 0), AW4_LUT_BINS - 1);
-    const int k = s.lut[b];
-    const float2 t = s.thr2[k];
-    return k + (x >= t.y ? 1 : 0) - (x < t.x ? 1 : 0);
+// Table search of a finite normalised value x in [-1, 1]: the stored code
+// (RTN) or the searchsorted-left index (SR); with levels, also the level of
+// that code.  The edge index floor((x + 1) * 512) lands in the low mantissa
+// bits of x * 512 + (2^23 + 512) when the FMA rounds toward zero (x * 512 is
+// exact, the sum lies in [2^23, 2^23 + 1024] where float32 spacing is 1, and
+// truncation of a positive value is its floor).
+__device__ __forceinline__ int lut_bin(float x) {
+    return __float_as_int(__fmaf_rz(x, 512.0f, 8389120.0f)) - 0x4B000000;
+}
+__device__ __forceinline__ int lut_search(const SmemSchemeT<false>& s, float x, float* level) {
+    const float2 e = *reinterpret_cast<const float2*>(&s.tab[lut_bin(x)]);
+    *level = 0.0f;
+    return __float_as_int(e.y) + (x >= e.x ? 1 : 0);
+}
+__device__ __forceinline__ int lut_search(const SmemSchemeT<true>& s, float x, float* level) {
+    const float4 e = *reinterpret_cast<const float4*>(&s.tab[lut_bin(x)]);
+    const bool up = x >= e.x;
+    *level = up ? e.w : e.z;
+    return __float_as_int(e.y) + (up ? 1 : 0);
+}
+
+// Decodes 8 packed codes (one 32-bit word, value i in bits 4i..4i+3) to
+// cb[code] * scale.  The product is an FMA with a +0 addend: the same value
+// as the multiply (the scale is >= 0 and products cannot be -0 here), and an
+// FMA result cannot be contracted into a following add.
+template <class S>
+__device__ __forceinline__ void decode8(const S& s, uint32_t w, float scale, float v[8]) {
+    const unsigned long long ss = pk2(scale, scale), zz = pk2(0.0f, 0.0f);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float2 lv = s.pair[__byte_perm(w, 0, 0x4440 + j)];
+        unsigned long long r;
+        asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(pk2(lv.x, lv.y)), "l"(ss), "l"(zz));
+        upk2(r, v[2 * j], v[2 * j + 1]);
+    }
 }
 
 // torch.searchsorted(cb, x) (left): the ATen lower-bound loop, NaN -> 16.

@@ -76,18 +76,24 @@ __device__ __forceinline__ float2 eden_sums(const GroupCtx& g, const float np[8]
     return make_float2(num, den);
 }
 
-// Encodes the group's block.  v: this lane's 8 working values.  u: 8 uniforms
-// (SR modes).  Returns this lane's 8 codes packed as nibbles (value 8j+i in
-// bits 4i..4i+3, i.e. the reference's little-endian nibble order) and sets
-// *scale_out to the block scale to store (identical in all 16 lanes).
-template <int MODE>
+// Max of |v[i]| over a lane's 8 values (NaN-propagating, like torch.max).
+__device__ __forceinline__ float lane_absmax(const float v[8]) {
+    float a = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) a = max_nan(a, fabsf(v[i]));
+    return a;
+}
+
+// Encodes the group's block.  v: this lane's 8 working values; amax: their
+// lane_absmax.  u: 8 uniforms (SR modes).  Returns this lane's 8 codes packed
+// as nibbles (value 8j+i in bits 4i..4i+3, i.e. the reference's little-endian
+// nibble order) and sets *scale_out to the block scale to store (identical
+// in all 16 lanes).
+template <int MODE, class SmemScheme>
 __device__ __forceinline__ uint32_t encode_block(const SmemScheme& S, const GroupCtx& g,
-                                                 const float v[8], const float u[8],
+                                                 const float v[8], float amax, const float u[8],
                                                  int zero_floor, int eden, float sr_bias,
                                                  float sr_eps, float* scale_out) {
-    float amax = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) amax = max_nan(amax, fabsf(v[i]));
     amax = group_max16(amax);
     const float sc = max_nan(amax, kScaleFloor);
     const bool fin = is_finite(sc);
@@ -95,32 +101,58 @@ __device__ __forceinline__ uint32_t encode_block(const SmemScheme& S, const Grou
         g.levels[g.j] = precond(sc, S.cb[g.j], sr_bias, sr_eps);
         __syncwarp();
     }
-    float x[8];
+    // x = v / scale, correctly rounded (Markstein when its preconditions
+    // hold).  A nonzero |v| < 2^-100 gives |x| < 2^-99, which every supported
+    // codebook rounds (RTN) to the code of 0 whatever its last bits, so RTN
+    // without EDEN needs no guard for it.
+    float x[8], q[8];
     int code[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-        x[i] = fdiv(v[i], sc);
-        if (MODE == AW4_RTN) {
-            code[i] = fin ? lut_search(S, x[i]) : rtn_literal(S.cb, x[i]);
+    if (fin) {
+        const bool need_guard = (MODE != AW4_RTN) || eden;
+        if (sc <= kMarksteinMaxDivisor && !(need_guard && any_tiny(v))) {
+            vdiv_markstein8(x, v, sc, frcp(sc));
         } else {
-            const int idx = fin ? lut_search(S, x[i]) : searchsorted_left(S.cb, x[i]);
-            if (MODE == AW4_SR_VALUE)
-                code[i] = value_sr_from_index(S.cb, idx, x[i], u[i]);
-            else
-                code[i] = update_sr_from_index(S.cb, g.levels, idx, x[i], sc, sr_bias, sr_eps,
-                                               u[i]);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) x[i] = fdiv(v[i], sc);
         }
-        if (zero_floor) code[i] = max(code[i], 1);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int idx = lut_search(S, x[i], &q[i]);
+            if (MODE == AW4_RTN) {
+                code[i] = idx;  // the dyn4_nz floor is folded into the RTN table
+            } else {
+                code[i] = (MODE == AW4_SR_VALUE)
+                              ? value_sr_from_index(S.cb, idx, x[i], u[i])
+                              : update_sr_from_index(S.cb, g.levels, idx, x[i], sc, sr_bias,
+                                                     sr_eps, u[i]);
+                if (zero_floor) code[i] = max(code[i], 1);
+                q[i] = S.cb[code[i]];
+            }
+        }
+    } else {
+        // non-finite block (NaN/inf moments): the literal reference rules
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            x[i] = fdiv(v[i], sc);
+            if (MODE == AW4_RTN) {
+                code[i] = rtn_literal(S.cb, x[i]);
+            } else {
+                const int idx = searchsorted_left(S.cb, x[i]);
+                code[i] = (MODE == AW4_SR_VALUE)
+                              ? value_sr_from_index(S.cb, idx, x[i], u[i])
+                              : update_sr_from_index(S.cb, g.levels, idx, x[i], sc, sr_bias,
+                                                     sr_eps, u[i]);
+            }
+            if (zero_floor) code[i] = max(code[i], 1);
+            q[i] = S.cb[code[i]];
+        }
     }
     if (MODE == AW4_SR_UPDATE) __syncwarp();  // level table reused by the next block
     float s = sc;
     if (eden) {
         float np[8], dp[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            np[i] = fmul(x[i], x[i]);
-            dp[i] = fmul(x[i], S.cb[code[i]]);
-        }
+        vmul8(np, x, x);
+        vmul8(dp, x, q);
         const float2 nd = eden_sums(g, np, dp);
         s = fmul(sc, fdiv(nd.x, max_nan(nd.y, kScaleFloor)));
     }

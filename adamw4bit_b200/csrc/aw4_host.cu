@@ -8,10 +8,12 @@
 // t_k = min{x : code(x) >= k}, found here by bisection over the ordered
 // float32 line with the literal rule.  For SR the search needs the
 // searchsorted index itself, i = #{k : cb[k] < x} = #{k : x >= nextup(cb[k])}.
-// A 2048-bin table over [-1, 1] then gives each bin's count of thresholds at
-// its lower edge; the kernels correct the (at most one) threshold inside the
-// bin with two compares.  The tables are verified against the literal rule
-// before they are returned.
+// A 1024-bin table over [-1, 1] then gives each bin's count of thresholds at
+// its lower edge.  The kernels compute the bin exactly, floor((x + 1) * 512),
+// with a round-toward-zero FMA (x * 512 is exact and rounding toward zero
+// never crosses an integer), so one compare against the next threshold
+// finishes the search as long as no bin holds two thresholds.  The tables are
+// verified against the literal rule before they are returned.
 #include <cuda_runtime.h>
 
 #include <atomic>
@@ -77,15 +79,19 @@ static int rtn_literal(const float* cb, float x) {
     return dl < dr ? l : r;
 }
 
-// Host copy of the kernels' table search.
+// Host copy of the kernels' table search (x in [-1, 1]); edge 1024 (x == 1)
+// extends the last bin's count by the threshold it may hold.
 static int lut_search(const aw4_scheme& s, float x) {
-    volatile float t = x * 1024.0f;  // exact (power-of-two scale)
-    volatile float y = t + 1024.0f;  // one rounding, as the device FMA
-    int b = (int)y;
-    if (b < 0) b = 0;
-    if (b > AW4_LUT_BINS - 1) b = AW4_LUT_BINS - 1;
-    const int k = s.lut[b];
-    return k + (x >= s.thr[k + 1] ? 1 : 0) - (x < s.thr[k] ? 1 : 0);
+    volatile float t = x * 512.0f;   // exact (power-of-two scale)
+    const int b = (int)std::floor(t) + 512;
+    int k;
+    if (b < AW4_LUT_BINS) {
+        k = s.lut[b];
+    } else {
+        k = s.lut[AW4_LUT_BINS - 1];
+        k += (s.thr[k + 1] <= 1.0f) ? 1 : 0;
+    }
+    return k + (x >= s.thr[k + 1] ? 1 : 0);
 }
 
 static int expected(const aw4_scheme& s, float x) {
@@ -142,12 +148,12 @@ extern "C" int32_t aw4_scheme_prepare(const float* cb, int32_t round_mode, int32
         for (int k = 0; k < 16; ++k) s.thr[k + 1] = std::nextafter(cb[k], INFINITY);
     }
     for (int k = nthr + 1; k < 18; ++k) s.thr[k] = INFINITY;
-    // at most one threshold per two bins, so one correction step suffices
+    // no two thresholds closer than a bin width, so no bin holds two
     for (int k = 1; k < nthr; ++k)
-        if ((double)s.thr[k + 1] - (double)s.thr[k] <= 2.0 / 1024.0)
+        if ((double)s.thr[k + 1] - (double)s.thr[k] <= 2.0 / AW4_LUT_BINS)
             return fail(AW4_ERR_UNSUPPORTED, "codebook levels too close for the search table");
     for (int b = 0; b < AW4_LUT_BINS; ++b) {
-        const float edge = -1.0f + (float)b / 1024.0f;  // exact
+        const float edge = -1.0f + (float)b / 512.0f;  // exact
         int count = 0;
         for (int k = 1; k <= nthr; ++k) count += (s.thr[k] <= edge) ? 1 : 0;
         s.lut[b] = (uint8_t)count;
@@ -164,7 +170,7 @@ extern "C" int32_t aw4_scheme_prepare(const float* cb, int32_t round_mode, int32
         }
     }
     for (int b = 0; b <= AW4_LUT_BINS; ++b) {
-        const int64_t c = fkey(-1.0f + (float)b / 1024.0f);
+        const int64_t c = fkey(-1.0f + (float)b / 512.0f);
         for (int64_t d = -8; d <= 8; ++d) {
             const float x = keyf(c + d);
             if (x < -1.0f || x > 1.0f) continue;

@@ -29,7 +29,7 @@
 
 namespace aw4 {
 
-constexpr int kMaxTensors = 224;   // tensors per launch (kernel parameter space)
+constexpr int kMaxTensors = 300;   // tensors per launch (kernel parameter space)
 constexpr int kMaxHypers = 8;      // distinct per-step scalar sets per launch
 
 struct KDesc {
@@ -51,15 +51,20 @@ struct KDesc {
 struct StepLaunch {
     aw4_scheme m1, m2;
     aw4_hyper hyper[kMaxHypers];
+    float rcp_sqrt_bc2[kMaxHypers];   // RN(1 / sqrt_bc2), IEEE division on the host
     int32_t n_tensors, n_tiles, eden, pad;
     KDesc t[kMaxTensors];
 };
 static_assert(sizeof(StepLaunch) <= 32000, "kernel parameter space");
 
 struct StepSmem {
-    SmemScheme s1, s2;
+    SmemSchemeT<false> s1;   // m1: no EDEN, no levels needed
+    SmemSchemeT<true> s2;
     float scratch[kThreads / 32][kWarpScratch];
 };
+// 16-byte table reads (s2), and float4 rows in each warp's EDEN scratch
+static_assert(offsetof(StepSmem, s2) % 16 == 0, "");
+static_assert(offsetof(StepSmem, scratch) % 16 == 0 && (kWarpScratch * 4) % 16 == 0, "");
 
 __device__ __forceinline__ int find_tensor(const StepLaunch& L, int tile) {
     int lo = 0, hi = L.n_tensors - 1;
@@ -71,7 +76,7 @@ __device__ __forceinline__ int find_tensor(const StepLaunch& L, int tile) {
 }
 
 template <int PT, int GT, int M1, int M2>
-__global__ void __launch_bounds__(kThreads)
+__global__ void __launch_bounds__(kThreads, 4)
 step_kernel(const __grid_constant__ StepLaunch L) {
     __shared__ __align__(16) StepSmem sm;
     const int tid = threadIdx.x;
@@ -84,8 +89,11 @@ step_kernel(const __grid_constant__ StepLaunch L) {
     const int group = tid >> 4;
     const int zf2 = L.m2.zero_floor;
 
+    // tiles only grow along this loop, so the owning tensor moves forward
+    int ti = find_tensor(L, blockIdx.x);
     for (int tile = blockIdx.x; tile < L.n_tiles; tile += gridDim.x) {
-        const KDesc& D = L.t[find_tensor(L, tile)];
+        while (ti + 1 < L.n_tensors && L.t[ti + 1].tile_begin <= tile) ++ti;
+        const KDesc& D = L.t[ti];
         const aw4_hyper& H = L.hyper[D.hyper];
         const int blk = (tile - D.tile_begin) * kBlocksPerTile + group;
         const bool active = blk < D.nblocks;
@@ -105,18 +113,38 @@ step_kernel(const __grid_constant__ StepLaunch L) {
 #pragma unroll
             for (int i = 0; i < 8; ++i) p[i] = gr[i] = 0.0f;
         }
+        // Packed f32x2 ops are used only where operand fusion cannot change a
+        // result (FMA, and products consumed by an FMA, a division or a store):
+        // ptxas may contract a packed mul.rn feeding a packed add/sub.rn into
+        // one FMA, so every multiply -> add/sub chain below stays scalar.
+        // decode (quantization.py:996-999)
+        float d[8], t[8];
+        decode8(sm.s1, w1, s1, m1);
+        decode8(sm.s2, w2, s2, m2);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) d[i] = fsub(gr[i], m1[i]);
+        vfmas8(m1, H.w1, d, m1);                 // m1.lerp_(g, 1-b1)  (adamw.py:557)
+#pragma unroll
+        for (int i = 0; i < 8; ++i) d[i] = fsub(fmul(gr[i], gr[i]), m2[i]);
+        vfmas8(m2, H.w2, d, m2);                 // m2.lerp_(g*g, 1-b2) (adamw.py:684)
+        const float amax2 = lane_absmax(m2);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) t[i] = fsqrt(m2[i]);
+        // den = sqrt(m2) / sqrt(bc2) + eps (adamw.py:685); sqrt of a finite
+        // float is 0 or >= 2^-75, so Markstein's preconditions hold
+        if (is_finite(amax2) && H.sqrt_bc2 >= kMarksteinMinDivisor &&
+            H.sqrt_bc2 <= kMarksteinMaxDivisor) {
+            vdiv_markstein8(d, t, H.sqrt_bc2, L.rcp_sqrt_bc2[D.hyper]);
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) d[i] = fdiv(t[i], H.sqrt_bc2);
+        }
+        vmuls8(t, m1, H.neg_step);               // (-lr/bc1) * m1, consumed by a division
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            // decode (quantization.py:996-999)
-            m1[i] = fmul(sm.s1.cb[(w1 >> (4 * i)) & 15u], s1);
-            m2[i] = fmul(sm.s2.cb[(w2 >> (4 * i)) & 15u], s2);
-            // AdamW in FP32 (adamw.py:557, 684-691, 743)
-            m1[i] = ffma(H.w1, fsub(gr[i], m1[i]), m1[i]);
-            const float gsq = fmul(gr[i], gr[i]);
-            m2[i] = ffma(H.w2, fsub(gsq, m2[i]), m2[i]);
-            const float den = fadd(fdiv(fsqrt(m2[i]), H.sqrt_bc2), H.eps);
-            const float pd = Elem<PT>::round(fmul(p[i], H.decay));
-            p[i] = fadd(pd, fdiv(fmul(H.neg_step, m1[i]), den));
+            const float den = fadd(d[i], H.eps);
+            const float pd = Elem<PT>::round(fmul(p[i], H.decay));   // p.mul_(1 - lr*wd)
+            p[i] = fadd(pd, fdiv(t[i], den));                       // p.addcdiv_(m1, den, -lr/bc1)
         }
         if (active) Elem<PT>::store8(D.param, e0, p);
 
@@ -133,7 +161,8 @@ step_kernel(const __grid_constant__ StepLaunch L) {
             }
         }
         float ns1;
-        const uint32_t c1 = encode_block<M1>(sm.s1, g, m1, u, 0, 0, H.sr_bias, H.eps, &ns1);
+        const uint32_t c1 =
+            encode_block<M1>(sm.s1, g, m1, lane_absmax(m1), u, 0, 0, H.sr_bias, H.eps, &ns1);
 
         // re-encode m2 (adamw.py:675-683 update-SR, 795-803 RTN + floor + EDEN)
         if (M2 != AW4_RTN) {
@@ -147,7 +176,8 @@ step_kernel(const __grid_constant__ StepLaunch L) {
             }
         }
         float ns2;
-        const uint32_t c2 = encode_block<M2>(sm.s2, g, m2, u, zf2, L.eden, H.sr_bias, H.eps, &ns2);
+        const uint32_t c2 =
+            encode_block<M2>(sm.s2, g, m2, amax2, u, zf2, L.eden, H.sr_bias, H.eps, &ns2);
 
         if (active) {
             __stcs(reinterpret_cast<unsigned int*>(D.c1 + (e0 >> 1)), c1);
@@ -344,6 +374,9 @@ extern "C" int32_t aw4_step_quantized(const aw4_scheme* m1, const aw4_scheme* m2
                 h = nh++;
                 hsrc.push_back(t.hyper);
                 L->hyper[h] = hypers[t.hyper];
+                // IEEE float32 division (SSE on the host): correctly rounded
+                volatile float one = 1.0f;
+                L->rcp_sqrt_bc2[h] = one / hypers[t.hyper].sqrt_bc2;
             }
             (void)hmap;
             KDesc& d = L->t[L->n_tensors++];

@@ -187,6 +187,10 @@ class QuantizedAdamW(Optimizer):
         # fused launch appends (start_event, end_event, numel) recorded on the
         # launching stream right around the native call.
         self.launch_timings: list | None = None
+        # Test hook: {id(param): (m1_uniforms, m2_uniforms)} device tensors fed
+        # to the kernel instead of the configured stream (for parity with the
+        # reference's own draws).
+        self._draws_override: dict | None = None
         self._check_groups()
 
     def _check_groups(self) -> None:
@@ -475,7 +479,12 @@ class _StepPlan:
         m1_sr = SCHEMES[m1].round_mode != N.RTN
         m2_sr = SCHEMES[m2].round_mode != N.RTN
         d1 = d2 = None
-        if opt._quant_rng == "torch":
+        override = opt._draws_override
+        if override is not None and id(p) in override:
+            # test hook: explicit uniforms (e.g. the reference's CPU draws)
+            d1, d2 = override[id(p)]
+            keys = (0, 0)
+        elif opt._quant_rng == "torch":
             d1, d2 = self._torch_draws(p, first, m1, m2, m1_sr, m2_sr)
             keys = (0, 0)
         else:

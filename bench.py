@@ -215,6 +215,8 @@ def run_ours(args, rank, world, local):
     shapes = llama3_8b_shapes()
     if args.layers is not None:
         shapes = shapes[:1 + 9 * args.layers] + shapes[-2:]
+    if args.values:
+        shapes = [(args.values,)]   # single-tensor case (profiling)
     total = sum(int(torch.Size(s).numel()) for s in shapes)
     params, grads = make_workload(dev, shapes)
     if world == 1:
@@ -343,7 +345,10 @@ def main():
     ap.add_argument("--cpu-sample", type=int, default=1 << 27,
                     help="values in the CPU-oracle sample (0: skip)")
     ap.add_argument("--cpu-steps", type=int, default=3)
-    ap.add_argument("--layers", type=int, default=None, help="debug: fewer decoder layers")
+    ap.add_argument("--layers", type=int, default=None, help="fewer decoder layers (smaller case)")
+    ap.add_argument("--values", type=int, default=0,
+                    help="one tensor of this many values instead of the Llama-3-8B set "
+                         "(small profiling case)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)

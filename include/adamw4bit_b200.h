@@ -39,7 +39,7 @@ extern "C" {
 
 #define AW4_ABI_VERSION 1
 #define AW4_BLOCK 128          /* elements per quantization block (4-bit default) */
-#define AW4_LUT_BINS 2048      /* uniform bins over [-1, 1] for the rounding search */
+#define AW4_LUT_BINS 1024      /* uniform bins over [-1, 1] for the rounding search */
 
 typedef enum aw4_status {
     AW4_OK = 0,
@@ -63,8 +63,9 @@ typedef struct aw4_scheme {
     float codebook[16];            /* sorted levels, bit-exact reference table */
     int32_t round_mode;            /* aw4_round */
     int32_t zero_floor;            /* 1: code 0 is stored as code 1 (dyn4_nz) */
-    /* rounding search: x in bin b = floor((x + 1) * 1024) has
-     * code = lut[b] + (x >= thr[lut[b] + 1]) - (x < thr[lut[b]]) */
+    /* rounding search: x in bin b = min(floor((x + 1) * 512), 1023) has
+     * code = lut[b] + (x >= thr[lut[b] + 1]); lut[b] counts the thresholds
+     * at or below the bin's lower edge, and no bin holds two thresholds */
     uint8_t lut[AW4_LUT_BINS];
     float thr[18];                 /* thr[0] = -inf, thr[last] = +inf */
     float zero_scale;              /* block scale stored for an all-zero block */

@@ -11,6 +11,8 @@ Bars (from the build's north star):
 
 from __future__ import annotations
 
+import zlib
+
 import numpy as np
 import pytest
 import torch
@@ -35,17 +37,29 @@ def _dev_from_np(a: np.ndarray, dtype: torch.dtype) -> torch.Tensor:
     return torch.from_numpy(a.view(np.int16).copy()).view(dtype).to(DEV)
 
 
+def assert_bits_equal(got: np.ndarray, want: np.ndarray, what: str, dtype=torch.float32):
+    """Bit-exact equality, except that any NaN equals any NaN (payloads and
+    signs of NaN differ between the GPU's and the CPU's conversions)."""
+    if dtype == torch.float32:
+        g, w = got.view(np.float32), want.view(np.float32)
+        gb, wb = got.view(np.uint32), want.view(np.uint32)
+    else:
+        g = torch.from_numpy(got.view(np.int16)).view(dtype).float().numpy()
+        w = torch.from_numpy(want.view(np.int16)).view(dtype).float().numpy()
+        gb, wb = got.view(np.uint16), want.view(np.uint16)
+    same = (gb == wb) | (np.isnan(g) & np.isnan(w))
+    if not same.all():
+        idx = np.nonzero(~same)[0]
+        raise AssertionError(f"{what}: {idx.size} of {same.size} differ; first {idx[:5]}: "
+                             f"got {g[idx[:5]]} want {w[idx[:5]]}")
+
+
 def _assert_state_equal(st: A.QTensorState, c1, s1, c2, s2, p_np, what=""):
     np.testing.assert_array_equal(A.to_np_bits(st.m1_codes), c1, err_msg=f"m1 codes {what}")
     np.testing.assert_array_equal(A.to_np_bits(st.m2_codes), c2, err_msg=f"m2 codes {what}")
-    np.testing.assert_array_equal(A.to_np_bits(st.m1_scales).view(np.uint32), s1.view(np.uint32),
-                                  err_msg=f"m1 scales {what}")
-    np.testing.assert_array_equal(A.to_np_bits(st.m2_scales).view(np.uint32), s2.view(np.uint32),
-                                  err_msg=f"m2 scales {what}")
-    got = A.to_np_bits(st.param)
-    np.testing.assert_array_equal(got.view(np.uint32) if got.dtype == np.float32 else got,
-                                  p_np.view(np.uint32) if p_np.dtype == np.float32 else p_np,
-                                  err_msg=f"params {what}")
+    assert_bits_equal(A.to_np_bits(st.m1_scales), s1, f"m1 scales {what}")
+    assert_bits_equal(A.to_np_bits(st.m2_scales), s2, f"m2 scales {what}")
+    assert_bits_equal(A.to_np_bits(st.param), p_np, f"params {what}", st.param.dtype)
 
 
 def _rand_inputs(rng, n, p_dtype, g_dtype, scale_spread=True):
@@ -84,7 +98,7 @@ DTYPES = [(torch.float32, torch.float32), (torch.float32, torch.bfloat16),
 def test_multi_tensor_step_matches_oracle_bit_exact(m1, m2, eden, p_dtype, g_dtype):
     """Several tensors (ragged tiles, a shard with an element offset) in one
     launch, 3 steps, in-kernel Philox for SR: bit-exact against the oracle."""
-    rng = np.random.default_rng(hash((m1, m2, eden, str(p_dtype), str(g_dtype))) % 2**32)
+    rng = np.random.default_rng(zlib.crc32(f"{m1}/{m2}/{eden}/{p_dtype}/{g_dtype}".encode()))
     sizes = [4096, 128 * 37, 2048 * 3 + 128, 16384]
     offsets = [0, 0, 128 * 5, 0]
     ordinals = [3, 0, 7, 1]

@@ -38,20 +38,21 @@ def test_library_loads_and_exports_every_declared_symbol():
 
 def test_struct_layouts_match_header():
     # sizes follow from the C declarations (natural alignment, x86-64)
-    assert ctypes.sizeof(N.Scheme) == 64 + 8 + 2048 + 72 + 8 + 4
+    assert ctypes.sizeof(N.Scheme) == 64 + 8 + N.LUT_BINS + 72 + 8 + 4
     assert ctypes.sizeof(N.Hyper) == 48
     assert ctypes.sizeof(N.QTensor) == 88
     assert ctypes.sizeof(N.FTensor) == 48
 
 
 def _lut_search(s: N.Scheme, x: np.ndarray) -> np.ndarray:
-    """numpy copy of the kernels' table search."""
+    """numpy copy of the kernels' table search: exact bin floor((x+1)*512)."""
     lut = np.frombuffer(bytes(s.lut), dtype=np.uint8)
     thr = np.array(list(s.thr), dtype=np.float32)
-    y = (x.astype(np.float32) * np.float32(1024.0) + np.float32(1024.0)).astype(np.float32)
-    b = np.clip(np.trunc(y).astype(np.int64), 0, N.LUT_BINS - 1)
-    k = lut[b].astype(np.int64)
-    return k + (x >= thr[k + 1]).astype(np.int64) - (x < thr[k]).astype(np.int64)
+    b = np.floor(x.astype(np.float32) * np.float32(512.0)).astype(np.int64) + 512
+    last = int(lut[N.LUT_BINS - 1])
+    lut = np.append(lut.astype(np.int64), last + int(thr[last + 1] <= 1.0))   # edge x == 1
+    k = lut[b]
+    return k + (x >= thr[k + 1]).astype(np.int64)
 
 
 def _literal_rtn(cb: np.ndarray, x: np.ndarray) -> np.ndarray:
