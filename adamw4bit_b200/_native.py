@@ -31,6 +31,7 @@ class Scheme(ctypes.Structure):
         ("codebook", ctypes.c_float * 16),
         ("round_mode", ctypes.c_int32),
         ("zero_floor", ctypes.c_int32),
+        ("lut_bins", ctypes.c_int32),
         ("lut", ctypes.c_uint8 * LUT_BINS),
         ("thr", ctypes.c_float * 18),
         ("zero_scale", ctypes.c_float),
@@ -84,8 +85,8 @@ SIGNATURES = {
     "aw4_launch_count": ([], _U64),
     "aw4_scheme_prepare": ([_VP, _I32, _I32, ctypes.POINTER(Scheme)], _I32),
     "aw4_step_quantized": ([ctypes.POINTER(Scheme), ctypes.POINTER(Scheme), _I32, _I32, _I32,
-                            ctypes.POINTER(QTensor), _I32, ctypes.POINTER(Hyper), _I32, _I32, _VP],
-                           _I32),
+                            ctypes.POINTER(QTensor), _I32, ctypes.POINTER(Hyper), _I32, _I32, _I32,
+                            _VP], _I32),
     "aw4_step_fp32_state": ([_I32, _I32, ctypes.POINTER(FTensor), _I32, ctypes.POINTER(Hyper),
                              _I32, _I32, _VP], _I32),
     "aw4_init_zero_state": ([ctypes.POINTER(Scheme), _I32, _VP, _VP, _I64, _I32, _VP], _I32),

@@ -26,11 +26,12 @@ __global__ void __launch_bounds__(kThreads)
 quantize_kernel(const __grid_constant__ aw4_scheme scheme, int eden, const float* x,
                 int64_t n_blocks, uint8_t* codes, float* scales, const float* draws,
                 uint64_t key, uint32_t step, uint32_t ordinal, float sr_bias, float sr_eps) {
-    __shared__ __align__(16) SmemSchemeT<true> S;
+    __shared__ __align__(16) SmemScheme S;
     __shared__ __align__(16) float scratch[kThreads / 32][kWarpScratch];
     load_scheme(S, scheme, threadIdx.x, kThreads);
     __syncthreads();
     const GroupCtx g = group_ctx(scratch[threadIdx.x >> 5], threadIdx.x & 31);
+    const SchemeRegs R = scheme_regs(S, threadIdx.x & 31);
     const int group = threadIdx.x >> 4;
     const int64_t n_tiles = (n_blocks + kBlocksPerTile - 1) / kBlocksPerTile;
     for (int64_t tile = blockIdx.x; tile < n_tiles; tile += gridDim.x) {
@@ -52,7 +53,7 @@ quantize_kernel(const __grid_constant__ aw4_scheme scheme, int eden, const float
             }
         }
         float s;
-        const uint32_t c = encode_block<MODE>(S, g, v, lane_absmax(v), u, scheme.zero_floor, eden,
+        const uint32_t c = encode_block<MODE>(S, R, g, v, lane_absmax(v), u, scheme.zero_floor, eden,
                                               sr_bias, sr_eps, &s);
         if (active) {
             reinterpret_cast<uint32_t*>(codes)[e0 >> 3] = c;

@@ -262,97 +262,94 @@ __device__ __forceinline__ void philox_uniform8(uint64_t key, uint32_t step, uin
 // ---------------------------------------------------------------------------
 // Rounding search (tables built by aw4_scheme_prepare)
 // ---------------------------------------------------------------------------
-// Rounding-search entry for bin edge b (x = -1 + b/512): the next threshold
-// above the edge and the code at the edge; the EDEN flavour also carries the
-// levels of that code and the next one.  For RTN schemes with the dyn4_nz
+// Rounding-search entry for bin edge b (x = -1 + 2b/N): the next threshold
+// above the edge and the code at the edge.  For RTN schemes with the dyn4_nz
 // floor the floor is folded in: codes below 1 read as 1.
 struct __align__(8) SearchEntry {
     float next_thr;
     int code;
 };
-struct __align__(16) SearchEntryL {
-    float next_thr;
-    int code;
-    float level;
-    float level_next;
-};
+static_assert(sizeof(SearchEntry) == 8, "");
 
-template <bool LEVELS>
-struct __align__(16) SmemSchemeT {
-    typename std::conditional<LEVELS, SearchEntryL, SearchEntry>::type tab[AW4_LUT_BINS + 1];
+struct __align__(16) SmemScheme {
+    SearchEntry tab[AW4_LUT_BINS + 1];   // the first lut_bins + 1 entries are used
     float cb[16];
-    float2 pair[256];  // packed code byte -> (cb[low nibble], cb[high nibble])
+    float half_bins;                      // lut_bins / 2
+    float bias;                           // 2^23 + lut_bins / 2
 };
-// lut_search reads entries as float2 / float4 and decode8 reads pairs as float2
-static_assert(alignof(SmemSchemeT<true>) == 16 && alignof(SmemSchemeT<false>) == 16, "");
-static_assert(sizeof(SearchEntryL) == 16 && sizeof(SearchEntry) == 8, "");
-static_assert(offsetof(SmemSchemeT<true>, pair) % 8 == 0, "");
-static_assert(offsetof(SmemSchemeT<false>, pair) % 8 == 0, "");
 
-template <bool LEVELS>
-__device__ __forceinline__ void load_scheme(SmemSchemeT<LEVELS>& s, const aw4_scheme& g,
-                                            int tid, int nthreads) {
+__device__ __forceinline__ void load_scheme(SmemScheme& s, const aw4_scheme& g, int tid,
+                                            int nthreads) {
     const bool floor_in_table = g.zero_floor && g.round_mode == AW4_RTN;
-    for (int b = tid; b <= AW4_LUT_BINS; b += nthreads) {
+    const int nb = g.lut_bins;
+    for (int b = tid; b <= nb; b += nthreads) {
         int k;
-        if (b < AW4_LUT_BINS) {
+        if (b < nb) {
             k = g.lut[b];
         } else {  // edge x = 1.0: one more threshold may sit in the last bin
-            k = g.lut[AW4_LUT_BINS - 1];
+            k = g.lut[nb - 1];
             k += (g.thr[k + 1] <= 1.0f) ? 1 : 0;
         }
         float next = g.thr[k + 1];
         if (floor_in_table && k == 0) {
-            // code(x) = max(0 + (x >= t1), 1) = 1 on this whole bin: the only
-            // threshold a bin can hold is t1, which moves no floored code
+            // no threshold is at or below this bin's edge, so at most t1 lies
+            // inside it, and max(code, 1) = 1 across the whole bin
             k = 1;
-            next = (g.thr[2] >= -1.0f + (float)(b + 1) / 512.0f) ? INFINITY : g.thr[2];
+            next = INFINITY;
         }
-        if constexpr (LEVELS) {
-            s.tab[b] = SearchEntryL{next, k, g.codebook[min(k, 15)], g.codebook[min(k + 1, 15)]};
-        } else {
-            s.tab[b] = SearchEntry{next, k};
-        }
+        s.tab[b] = SearchEntry{next, k};
     }
     for (int i = tid; i < 16; i += nthreads) s.cb[i] = g.codebook[i];
-    for (int i = tid; i < 256; i += nthreads)
-        s.pair[i] = make_float2(g.codebook[i & 15], g.codebook[i >> 4]);
+    if (tid == 0) {
+        s.half_bins = (float)(nb / 2);
+        s.bias = 8388608.0f + (float)(nb / 2);
+    }
+}
+
+// Per-lane register copies of a scheme's search constants and codebook level.
+struct SchemeRegs {
+    float cbv;    // cb[lane % 16], read by shuffles
+    float half;   // lut_bins / 2
+    float bias;   // 2^23 + lut_bins / 2
+};
+__device__ __forceinline__ SchemeRegs scheme_regs(const SmemScheme& s, int lane) {
+    return SchemeRegs{s.cb[lane & 15], s.half_bins, s.bias};
 }
 
 // Table search of a finite normalised value x in [-1, 1]: the stored code
-// (RTN) or the searchsorted-left index (SR); with levels, also the level of
-// that code.  The edge index floor((x + 1) * 512) lands in the low mantissa
-// bits of x * 512 + (2^23 + 512) when the FMA rounds toward zero (x * 512 is
-// exact, the sum lies in [2^23, 2^23 + 1024] where float32 spacing is 1, and
-// truncation of a positive value is its floor).
-__device__ __forceinline__ int lut_bin(float x) {
-    return __float_as_int(__fmaf_rz(x, 512.0f, 8389120.0f)) - 0x4B000000;
-}
-__device__ __forceinline__ int lut_search(const SmemSchemeT<false>& s, float x, float* level) {
-    const float2 e = *reinterpret_cast<const float2*>(&s.tab[lut_bin(x)]);
-    *level = 0.0f;
+// (RTN) or the searchsorted-left index (SR).  With N bins the edge index
+// floor((x + 1) * N / 2) lands in the low mantissa bits of
+// x * N/2 + (2^23 + N/2) when the FMA rounds toward zero (the power-of-two
+// product is exact, the sum lies in [2^23, 2^23 + N] where float32 spacing is
+// 1, and truncation of a positive value is its floor).
+__device__ __forceinline__ int lut_search(const SmemScheme& s, const SchemeRegs& r, float x) {
+    const int b = __float_as_int(__fmaf_rz(x, r.half, r.bias)) - 0x4B000000;
+    const float2 e = *reinterpret_cast<const float2*>(&s.tab[b]);
     return __float_as_int(e.y) + (x >= e.x ? 1 : 0);
 }
-__device__ __forceinline__ int lut_search(const SmemSchemeT<true>& s, float x, float* level) {
-    const float4 e = *reinterpret_cast<const float4*>(&s.tab[lut_bin(x)]);
-    const bool up = x >= e.x;
-    *level = up ? e.w : e.z;
-    return __float_as_int(e.y) + (up ? 1 : 0);
+
+// Level of a code from the codebook held in registers: lane l keeps
+// cbv = cb[l % 16], and a shuffle reads lane `code`.
+__device__ __forceinline__ float level_of(float cbv, int code) {
+    return __shfl_sync(0xffffffffu, cbv, code);
 }
 
 // Decodes 8 packed codes (one 32-bit word, value i in bits 4i..4i+3) to
-// cb[code] * scale.  The product is an FMA with a +0 addend: the same value
-// as the multiply (the scale is >= 0 and products cannot be -0 here), and an
-// FMA result cannot be contracted into a following add.
-template <class S>
-__device__ __forceinline__ void decode8(const S& s, uint32_t w, float scale, float v[8]) {
+// cb[code] * scale.  The shuffle source lane is taken modulo 32, and lanes l
+// and l + 16 hold the same level, so w >> 4i needs no mask.  The product is
+// an FMA with a +0 addend: the same value as the multiply (the scale is >= 0
+// and products cannot be -0 here), and an FMA result cannot be contracted
+// into a following add.
+__device__ __forceinline__ void decode8(float cbv, uint32_t w, float scale, float v[8]) {
+    float lv[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) lv[i] = __shfl_sync(0xffffffffu, cbv, (int)(w >> (4 * i)));
     const unsigned long long ss = pk2(scale, scale), zz = pk2(0.0f, 0.0f);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-        const float2 lv = s.pair[__byte_perm(w, 0, 0x4440 + j)];
+    for (int i = 0; i < 8; i += 2) {
         unsigned long long r;
-        asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(pk2(lv.x, lv.y)), "l"(ss), "l"(zz));
-        upk2(r, v[2 * j], v[2 * j + 1]);
+        asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(pk2(lv[i], lv[i + 1])), "l"(ss), "l"(zz));
+        upk2(r, v[i], v[i + 1]);
     }
 }
 

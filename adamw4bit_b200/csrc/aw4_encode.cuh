@@ -12,17 +12,20 @@
 namespace aw4 {
 
 // Per-warp scratch for EDEN sums and the update-SR level table.
-// EDEN: four 136-float tables (num/den x 2 groups); the 8-float pad between
-// tables puts the 32 lanes' column reads on 32 distinct banks.
-constexpr int kEdenTable = 136;
-constexpr int kWarpScratch = 4 * kEdenTable + 32 /* column totals */ + 32 /* level table */;
+// EDEN: four tables (num/den x the warp's 2 groups) of 16 rows x 12 floats
+// (8 products + 4 pad).  The 12-float rows make each quarter-warp's float4
+// row writes hit 32 distinct banks; tables 200 floats apart start 8 banks
+// apart, so the 32 lanes' column reads hit 32 distinct banks too.
+constexpr int kEdenRow = 12;
+constexpr int kEdenTable = 200;
+constexpr int kWarpScratch = 4 * kEdenTable + 32 /* update-SR level tables */;
 
 struct GroupCtx {
-    float* eden_num;   // this group's 128-float products table
+    float* eden_num;   // this group's products tables
     float* eden_den;
-    float* totals;     // 16 floats: 8 num column totals, 8 den column totals
     float* levels;     // 16 floats: update-SR preconditioner of each level
     int j;             // lane within the group (0..15)
+    int lane;          // lane within the warp
 };
 
 __device__ __forceinline__ GroupCtx group_ctx(float* warp_scratch, int lane) {
@@ -30,9 +33,9 @@ __device__ __forceinline__ GroupCtx group_ctx(float* warp_scratch, int lane) {
     GroupCtx g;
     g.eden_num = warp_scratch + (2 * h) * kEdenTable;
     g.eden_den = warp_scratch + (2 * h + 1) * kEdenTable;
-    g.totals = warp_scratch + 4 * kEdenTable + 16 * h;
-    g.levels = warp_scratch + 4 * kEdenTable + 32 + 16 * h;
+    g.levels = warp_scratch + 4 * kEdenTable + 16 * h;
     g.j = lane & 15;
+    g.lane = lane;
     return g;
 }
 
@@ -43,8 +46,8 @@ __device__ __forceinline__ GroupCtx group_ctx(float* warp_scratch, int lane) {
 // Returns (num, den) totals, valid in every lane of the group.
 __device__ __forceinline__ float2 eden_sums(const GroupCtx& g, const float np[8],
                                             const float dp[8]) {
-    float4* rn = reinterpret_cast<float4*>(g.eden_num + 8 * g.j);
-    float4* rd = reinterpret_cast<float4*>(g.eden_den + 8 * g.j);
+    float4* rn = reinterpret_cast<float4*>(g.eden_num + kEdenRow * g.j);
+    float4* rd = reinterpret_cast<float4*>(g.eden_den + kEdenRow * g.j);
     rn[0] = make_float4(np[0], np[1], np[2], np[3]);
     rn[1] = make_float4(np[4], np[5], np[6], np[7]);
     rd[0] = make_float4(dp[0], dp[1], dp[2], dp[3]);
@@ -56,23 +59,21 @@ __device__ __forceinline__ float2 eden_sums(const GroupCtx& g, const float np[8]
     float acc[4];
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-        float a = fadd(0.0f, tab[8 * k + c]);
-        a = fadd(a, tab[8 * (k + 4) + c]);
-        a = fadd(a, tab[8 * (k + 8) + c]);
-        a = fadd(a, tab[8 * (k + 12) + c]);
+        float a = fadd(0.0f, tab[kEdenRow * k + c]);
+        a = fadd(a, tab[kEdenRow * (k + 4) + c]);
+        a = fadd(a, tab[kEdenRow * (k + 8) + c]);
+        a = fadd(a, tab[kEdenRow * (k + 12) + c]);
         acc[k] = a;
     }
-    g.totals[g.j] = fadd(fadd(fadd(acc[0], acc[1]), acc[2]), acc[3]);
-    __syncwarp();
-    const float4* tn = reinterpret_cast<const float4*>(g.totals);
-    const float4 n0 = tn[0], n1 = tn[1], d0 = tn[2], d1 = tn[3];
-    float num = fadd(0.0f, n0.x);
-    num = fadd(num, n0.y); num = fadd(num, n0.z); num = fadd(num, n0.w);
-    num = fadd(num, n1.x); num = fadd(num, n1.y); num = fadd(num, n1.z); num = fadd(num, n1.w);
-    float den = fadd(0.0f, d0.x);
-    den = fadd(den, d0.y); den = fadd(den, d0.z); den = fadd(den, d0.w);
-    den = fadd(den, d1.x); den = fadd(den, d1.y); den = fadd(den, d1.z); den = fadd(den, d1.w);
-    __syncwarp();  // scratch is reused by the next block
+    const float t = fadd(fadd(fadd(acc[0], acc[1]), acc[2]), acc[3]);
+    __syncwarp();  // tables are reused by the next block
+    // column totals in order from zero: each lane chains its half's 8 totals
+    const int base = g.lane & 24;   // group base + numerator/denominator half
+    float chain = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) chain = fadd(chain, __shfl_sync(0xffffffffu, t, base + i));
+    const float num = __shfl_sync(0xffffffffu, chain, g.lane & 16);
+    const float den = __shfl_sync(0xffffffffu, chain, (g.lane & 16) | 8);
     return make_float2(num, den);
 }
 
@@ -89,8 +90,9 @@ __device__ __forceinline__ float lane_absmax(const float v[8]) {
 // as nibbles (value 8j+i in bits 4i..4i+3, i.e. the reference's little-endian
 // nibble order) and sets *scale_out to the block scale to store (identical
 // in all 16 lanes).
-template <int MODE, class SmemScheme>
-__device__ __forceinline__ uint32_t encode_block(const SmemScheme& S, const GroupCtx& g,
+template <int MODE>
+__device__ __forceinline__ uint32_t encode_block(const SmemScheme& S, const SchemeRegs& R,
+                                                 const GroupCtx& g,
                                                  const float v[8], float amax, const float u[8],
                                                  int zero_floor, int eden, float sr_bias,
                                                  float sr_eps, float* scale_out) {
@@ -117,7 +119,7 @@ __device__ __forceinline__ uint32_t encode_block(const SmemScheme& S, const Grou
         }
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-            const int idx = lut_search(S, x[i], &q[i]);
+            const int idx = lut_search(S, R, x[i]);
             if (MODE == AW4_RTN) {
                 code[i] = idx;  // the dyn4_nz floor is folded into the RTN table
             } else {
@@ -126,7 +128,6 @@ __device__ __forceinline__ uint32_t encode_block(const SmemScheme& S, const Grou
                               : update_sr_from_index(S.cb, g.levels, idx, x[i], sc, sr_bias,
                                                      sr_eps, u[i]);
                 if (zero_floor) code[i] = max(code[i], 1);
-                q[i] = S.cb[code[i]];
             }
         }
     } else {
@@ -144,13 +145,14 @@ __device__ __forceinline__ uint32_t encode_block(const SmemScheme& S, const Grou
                                                      sr_eps, u[i]);
             }
             if (zero_floor) code[i] = max(code[i], 1);
-            q[i] = S.cb[code[i]];
         }
     }
     if (MODE == AW4_SR_UPDATE) __syncwarp();  // level table reused by the next block
     float s = sc;
     if (eden) {
         float np[8], dp[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) q[i] = level_of(R.cbv, code[i]);
         vmul8(np, x, x);
         vmul8(dp, x, q);
         const float2 nd = eden_sums(g, np, dp);

@@ -8,12 +8,13 @@
 // t_k = min{x : code(x) >= k}, found here by bisection over the ordered
 // float32 line with the literal rule.  For SR the search needs the
 // searchsorted index itself, i = #{k : cb[k] < x} = #{k : x >= nextup(cb[k])}.
-// A 1024-bin table over [-1, 1] then gives each bin's count of thresholds at
-// its lower edge.  The kernels compute the bin exactly, floor((x + 1) * 512),
-// with a round-toward-zero FMA (x * 512 is exact and rounding toward zero
-// never crosses an integer), so one compare against the next threshold
-// finishes the search as long as no bin holds two thresholds.  The tables are
-// verified against the literal rule before they are returned.
+// A table of N uniform bins over [-1, 1] (N the fewest power of two, at most
+// 1024, for which no bin holds two thresholds) then gives each bin's count of
+// thresholds at its lower edge.  The kernels compute the bin exactly,
+// floor((x + 1) * N / 2), with a round-toward-zero FMA (the power-of-two
+// product is exact and rounding toward zero never crosses an integer), so
+// one compare against the next threshold finishes the search.  The tables
+// are verified against the literal rule before they are returned.
 #include <cuda_runtime.h>
 
 #include <atomic>
@@ -79,16 +80,17 @@ static int rtn_literal(const float* cb, float x) {
     return dl < dr ? l : r;
 }
 
-// Host copy of the kernels' table search (x in [-1, 1]); edge 1024 (x == 1)
+// Host copy of the kernels' table search (x in [-1, 1]); the edge at x == 1
 // extends the last bin's count by the threshold it may hold.
 static int lut_search(const aw4_scheme& s, float x) {
-    volatile float t = x * 512.0f;   // exact (power-of-two scale)
-    const int b = (int)std::floor(t) + 512;
+    const int half = s.lut_bins / 2;
+    volatile float t = x * (float)half;   // exact (power-of-two scale)
+    const int b = (int)std::floor(t) + half;
     int k;
-    if (b < AW4_LUT_BINS) {
+    if (b < s.lut_bins) {
         k = s.lut[b];
     } else {
-        k = s.lut[AW4_LUT_BINS - 1];
+        k = s.lut[s.lut_bins - 1];
         k += (s.thr[k + 1] <= 1.0f) ? 1 : 0;
     }
     return k + (x >= s.thr[k + 1] ? 1 : 0);
@@ -148,12 +150,21 @@ extern "C" int32_t aw4_scheme_prepare(const float* cb, int32_t round_mode, int32
         for (int k = 0; k < 16; ++k) s.thr[k + 1] = std::nextafter(cb[k], INFINITY);
     }
     for (int k = nthr + 1; k < 18; ++k) s.thr[k] = INFINITY;
-    // no two thresholds closer than a bin width, so no bin holds two
-    for (int k = 1; k < nthr; ++k)
-        if ((double)s.thr[k + 1] - (double)s.thr[k] <= 2.0 / AW4_LUT_BINS)
-            return fail(AW4_ERR_UNSUPPORTED, "codebook levels too close for the search table");
-    for (int b = 0; b < AW4_LUT_BINS; ++b) {
-        const float edge = -1.0f + (float)b / 512.0f;  // exact
+    // the fewest power-of-two bins for which no two thresholds are closer
+    // than a bin width, so that no bin holds two
+    double min_gap = INFINITY;
+    for (int k = 1; k < nthr; ++k) min_gap = std::fmin(min_gap, (double)s.thr[k + 1] - s.thr[k]);
+    s.lut_bins = 0;
+    for (int nb = 32; nb <= AW4_LUT_BINS; nb *= 2)
+        if (min_gap > 2.0 / nb) {
+            s.lut_bins = nb;
+            break;
+        }
+    if (s.lut_bins == 0)
+        return fail(AW4_ERR_UNSUPPORTED, "codebook levels too close for the search table");
+    const float half = (float)(s.lut_bins / 2);
+    for (int b = 0; b < s.lut_bins; ++b) {
+        const float edge = -1.0f + (float)b / half;  // exact
         int count = 0;
         for (int k = 1; k <= nthr; ++k) count += (s.thr[k] <= edge) ? 1 : 0;
         s.lut[b] = (uint8_t)count;
@@ -169,8 +180,8 @@ extern "C" int32_t aw4_scheme_prepare(const float* cb, int32_t round_mode, int32
                 return fail(AW4_ERR_UNSUPPORTED, "search table mismatch near threshold %d", k);
         }
     }
-    for (int b = 0; b <= AW4_LUT_BINS; ++b) {
-        const int64_t c = fkey(-1.0f + (float)b / 512.0f);
+    for (int b = 0; b <= s.lut_bins; ++b) {
+        const int64_t c = fkey(-1.0f + (float)b / half);
         for (int64_t d = -8; d <= 8; ++d) {
             const float x = keyf(c + d);
             if (x < -1.0f || x > 1.0f) continue;

@@ -58,8 +58,7 @@ struct StepLaunch {
 static_assert(sizeof(StepLaunch) <= 32000, "kernel parameter space");
 
 struct StepSmem {
-    SmemSchemeT<false> s1;   // m1: no EDEN, no levels needed
-    SmemSchemeT<true> s2;
+    SmemScheme s1, s2;
     float scratch[kThreads / 32][kWarpScratch];
 };
 // 16-byte table reads (s2), and float4 rows in each warp's EDEN scratch
@@ -86,6 +85,7 @@ step_kernel(const __grid_constant__ StepLaunch L) {
 
     const int lane = tid & 31;
     const GroupCtx g = group_ctx(sm.scratch[tid >> 5], lane);
+    const SchemeRegs r1 = scheme_regs(sm.s1, lane), r2 = scheme_regs(sm.s2, lane);
     const int group = tid >> 4;
     const int zf2 = L.m2.zero_floor;
 
@@ -119,8 +119,8 @@ step_kernel(const __grid_constant__ StepLaunch L) {
         // one FMA, so every multiply -> add/sub chain below stays scalar.
         // decode (quantization.py:996-999)
         float d[8], t[8];
-        decode8(sm.s1, w1, s1, m1);
-        decode8(sm.s2, w2, s2, m2);
+        decode8(r1.cbv, w1, s1, m1);
+        decode8(r2.cbv, w2, s2, m2);
 #pragma unroll
         for (int i = 0; i < 8; ++i) d[i] = fsub(gr[i], m1[i]);
         vfmas8(m1, H.w1, d, m1);                 // m1.lerp_(g, 1-b1)  (adamw.py:557)
@@ -162,7 +162,7 @@ step_kernel(const __grid_constant__ StepLaunch L) {
         }
         float ns1;
         const uint32_t c1 =
-            encode_block<M1>(sm.s1, g, m1, lane_absmax(m1), u, 0, 0, H.sr_bias, H.eps, &ns1);
+            encode_block<M1>(sm.s1, r1, g, m1, lane_absmax(m1), u, 0, 0, H.sr_bias, H.eps, &ns1);
 
         // re-encode m2 (adamw.py:675-683 update-SR, 795-803 RTN + floor + EDEN)
         if (M2 != AW4_RTN) {
@@ -177,7 +177,7 @@ step_kernel(const __grid_constant__ StepLaunch L) {
         }
         float ns2;
         const uint32_t c2 =
-            encode_block<M2>(sm.s2, g, m2, amax2, u, zf2, L.eden, H.sr_bias, H.eps, &ns2);
+            encode_block<M2>(sm.s2, r2, g, m2, amax2, u, zf2, L.eden, H.sr_bias, H.eps, &ns2);
 
         if (active) {
             __stcs(reinterpret_cast<unsigned int*>(D.c1 + (e0 >> 1)), c1);
@@ -307,8 +307,8 @@ using namespace aw4;
 extern "C" int32_t aw4_step_quantized(const aw4_scheme* m1, const aw4_scheme* m2, int32_t eden,
                                       int32_t param_dtype, int32_t grad_dtype,
                                       const aw4_qtensor* tensors, int32_t n_tensors,
-                                      const aw4_hyper* hypers, int32_t n_hypers, int32_t device,
-                                      void* stream) {
+                                      const aw4_hyper* hypers, int32_t n_hypers, int32_t max_ctas,
+                                      int32_t device, void* stream) {
     if (!m1 || !m2 || (n_tensors > 0 && (!tensors || !hypers)) || n_tensors < 0 || n_hypers < 0)
         return fail(AW4_ERR_INVALID, "aw4_step_quantized: null argument or negative count");
     if (m1->round_mode != AW4_RTN && m1->round_mode != AW4_SR_VALUE)
@@ -343,7 +343,8 @@ extern "C" int32_t aw4_step_quantized(const aw4_scheme* m1, const aw4_scheme* m2
     DeviceGuard guard(device);
     if (!guard.ok()) return fail(AW4_ERR_CUDA, "cudaSetDevice(%d) failed", device);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const int grid_cap = grid_for(fn, device, 1 << 30);
+    int grid_cap = grid_for(fn, device, 1 << 30);
+    if (max_ctas > 0) grid_cap = std::min(grid_cap, max_ctas);
 
     // Pack tensors into launches of <= kMaxTensors tensors / kMaxHypers scalar sets.
     StepLaunch* L = new StepLaunch;

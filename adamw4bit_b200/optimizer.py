@@ -556,7 +556,7 @@ class _StepPlan:
                 ev1 = torch.cuda.Event(enable_timing=True)
                 ev0.record(torch.cuda.current_stream(dev))
             N.check(N.lib().aw4_step_quantized(prepared(m1), prepared(m2), int(eden), pdt, gdt, tarr,
-                                               len(tensors), harr, len(hypers), dev.index,
+                                               len(tensors), harr, len(hypers), 0, dev.index,
                                                N.stream_handle(dev)), "aw4_step_quantized")
             if timing is not None:
                 ev1.record(torch.cuda.current_stream(dev))

@@ -94,11 +94,13 @@ class ZeRO1AdamW4Bit:
         process_group: NCCL group (default: the world).
         rounds: number of pipelined gather rounds.
         quant_rng_seed: Philox seed for SR recipes.
+        reserve_sms: SMs the update grid leaves to the concurrent all-gather.
     """
 
     def __init__(self, params, *, recipe: str = "ze-eden", lr: float = 1e-3,
                  betas=(0.9, 0.95), eps: float = 1e-8, weight_decay: float = 0.1,
-                 process_group=None, rounds: int = 4, quant_rng_seed: int = 0):
+                 process_group=None, rounds: int = 4, quant_rng_seed: int = 0,
+                 reserve_sms: int = 16):
         self.params = [p for p in params]
         if not self.params:
             raise ValueError("ZeRO1AdamW4Bit needs parameters")
@@ -146,6 +148,10 @@ class ZeRO1AdamW4Bit:
         self.step_count = 0
         self.segments = plan.segments
         self.gather_stream = torch.cuda.Stream(dev) if W > 1 else None
+        # With a concurrent all-gather, leave `reserve_sms` SMs free so NCCL's
+        # kernels can run beside the persistent update grid (4 CTAs per SM).
+        sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        self.max_ctas = max(1, (sms - reserve_sms) * 4) if W > 1 else 0
         self.launch_timings: list | None = None
 
     @torch.no_grad()
@@ -183,7 +189,7 @@ class ZeRO1AdamW4Bit:
                     e0.record(cur)
                 N.check(N.lib().aw4_step_quantized(prepared(self.m1), prepared(self.m2),
                                                    int(self.eden), pdt, gdt, arr, len(descs), harr,
-                                                   1, dev.index, cur.cuda_stream),
+                                                   1, self.max_ctas, dev.index, cur.cuda_stream),
                         "aw4_step_quantized")
                 if self.launch_timings is not None:
                     e1.record(cur)

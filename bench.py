@@ -278,7 +278,10 @@ def run_ours(args, rank, world, local):
                 "kernel": "aw4::step_kernel<F32,BF16,RTN,RTN> (fused decode+AdamW+encode)",
                 "launch_ms": round(per_launch_ms, 4), "values_per_launch": int(per_launch_elems)}
 
-    e2e = run_e2e(args, opt, params, grads, dev, world, total) if args.e2e_steps > 0 else None
+    e2e = None
+    if args.e2e_steps > 0:
+        e2e = (run_e2e(args, opt, params, grads, dev, world, total) if world == 1
+               else run_e2e_sharded(args, opt, params, grads, dev, world, total))
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
@@ -332,6 +335,41 @@ def run_e2e(args, opt, params, grads, dev, world, total):
     return {"value": total * args.e2e_steps / (ms / 1e3), "unit": UNIT,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "ms_per_step": ms / args.e2e_steps, "steps": args.e2e_steps}
+
+
+def run_e2e_sharded(args, opt, params, grads, dev, world, total):
+    """ZeRO-1 end to end: each rank copies in the gradient values it owns from
+    pinned host memory, steps (update + NCCL all-gather), and copies its
+    updated parameter shard back to pinned host memory."""
+    segs = [seg for round_segs in opt.segments for seg in round_segs]
+    host_g = [grads[ti].reshape(-1)[s:s + n].to("cpu").pin_memory() for ti, s, n, _ in segs]
+    owned = [(a, b) for a, b in opt.owned if b > a]
+    host_p = [torch.empty(b - a, dtype=opt.flat.dtype, pin_memory=True) for a, b in owned]
+    h2d = sum(h.numel() * h.element_size() for h in host_g)
+    d2h = sum(h.numel() * h.element_size() for h in host_p)
+    cur = torch.cuda.current_stream(dev)
+
+    def one():
+        for (ti, s, n, _), hg in zip(segs, host_g):
+            params[ti].grad.reshape(-1)[s:s + n].copy_(hg, non_blocking=True)
+        opt.step()
+        for (a, b), hp in zip(owned, host_p):
+            hp.copy_(opt.flat[a:b], non_blocking=True)
+
+    one()
+    barrier(world)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(cur)
+    for _ in range(args.e2e_steps):
+        one()
+    e1.record(cur)
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1), world)
+    return {"value": total * args.e2e_steps / (ms / 1e3), "unit": UNIT,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "bytes_are_per_rank": True, "ms_per_step": ms / args.e2e_steps,
+            "steps": args.e2e_steps}
 
 
 def main():

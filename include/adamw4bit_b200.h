@@ -39,7 +39,7 @@ extern "C" {
 
 #define AW4_ABI_VERSION 1
 #define AW4_BLOCK 128          /* elements per quantization block (4-bit default) */
-#define AW4_LUT_BINS 1024      /* uniform bins over [-1, 1] for the rounding search */
+#define AW4_LUT_BINS 1024      /* maximum uniform bins over [-1, 1] for the rounding search */
 
 typedef enum aw4_status {
     AW4_OK = 0,
@@ -63,9 +63,11 @@ typedef struct aw4_scheme {
     float codebook[16];            /* sorted levels, bit-exact reference table */
     int32_t round_mode;            /* aw4_round */
     int32_t zero_floor;            /* 1: code 0 is stored as code 1 (dyn4_nz) */
-    /* rounding search: x in bin b = min(floor((x + 1) * 512), 1023) has
-     * code = lut[b] + (x >= thr[lut[b] + 1]); lut[b] counts the thresholds
-     * at or below the bin's lower edge, and no bin holds two thresholds */
+    /* rounding search over lut_bins uniform bins of [-1, 1] (a power of two,
+     * the fewest for which no bin holds two thresholds): x in bin
+     * b = floor((x + 1) * lut_bins / 2) has code = lut[b] + (x >= thr[lut[b] + 1]);
+     * lut[b] counts the thresholds at or below the bin's lower edge */
+    int32_t lut_bins;
     uint8_t lut[AW4_LUT_BINS];
     float thr[18];                 /* thr[0] = -inf, thr[last] = +inf */
     float zero_scale;              /* block scale stored for an all-zero block */
@@ -127,11 +129,13 @@ int32_t aw4_scheme_prepare(const float* codebook16, int32_t round_mode, int32_t 
 /* Fused AdamW step over quantized tensors: decode NF4/Dyn4 codes, AdamW in
  * FP32, parameter update, re-encode with block absmax scales (RTN or SR, the
  * optional dyn4_nz floor and EDEN on m2) and write packed codes back.  All
- * tensors of one call share the param/grad dtypes and the two schemes. */
+ * tensors of one call share the param/grad dtypes and the two schemes.
+ * max_ctas > 0 caps the persistent grid (to leave SMs to a concurrent
+ * collective); 0 fills the GPU. */
 int32_t aw4_step_quantized(const aw4_scheme* m1, const aw4_scheme* m2, int32_t eden,
                            int32_t param_dtype, int32_t grad_dtype,
                            const aw4_qtensor* tensors, int32_t n_tensors,
-                           const aw4_hyper* hypers, int32_t n_hypers,
+                           const aw4_hyper* hypers, int32_t n_hypers, int32_t max_ctas,
                            int32_t device, void* stream);
 
 /* AdamW step over tensors that keep FP32 moments. */

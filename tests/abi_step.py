@@ -61,7 +61,7 @@ def step(states: list[QTensorState], grads: list[torch.Tensor], *, m1_scheme: st
     arr = (N.QTensor * n)(*descs)
     harr = (N.Hyper * len(hypers))(*hypers)
     N.check(N.lib().aw4_step_quantized(Q.prepared(m1_scheme), Q.prepared(m2_scheme), int(eden),
-                                       pdt, gdt, arr, n, harr, len(hypers), dev.index,
+                                       pdt, gdt, arr, n, harr, len(hypers), 0, dev.index,
                                        N.stream_handle(dev)), "aw4_step_quantized")
 
 

@@ -1,0 +1,85 @@
+"""ZeRO-1 sharded step on 2 GPUs (NCCL): every rank's parameters after the
+sharded update + all-gather are bit-identical to the unsharded single-GPU
+step.  Runs as two spawned child processes; skipped with fewer than 2 GPUs.
+NVLS is off for the test (NCCL_NVLS_ENABLE=0)."""
+
+from __future__ import annotations
+
+import os
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(4096,), (128, 96), (1024, 64), (8192,), (384, 256)]
+
+
+def _make(dev, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    params = [(torch.randn(s, generator=g) * 0.02).to(dev) for s in SHAPES]
+    grads = [[(torch.randn(s, generator=g) * 1e-3).to(dev, torch.bfloat16) for s in SHAPES]
+             for _ in range(3)]
+    return params, grads
+
+
+def _worker(rank, world, port, recipe, rounds, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import datetime
+
+    import torch.distributed as dist
+
+    from adamw4bit_b200 import ZEEDENAdamW4Bit, ZIPSRAdamW4Bit
+    from adamw4bit_b200.zero import ZeRO1AdamW4Bit
+    try:
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=120), device_id=dev)
+        vals, grads = _make(dev)
+        params = [torch.nn.Parameter(v.clone()) for v in vals]
+        for p in params:
+            p.grad_dtype = None
+        opt = ZeRO1AdamW4Bit(params, recipe=recipe, rounds=rounds, quant_rng_seed=9)
+        for step_grads in grads:
+            for p, g in zip(params, step_grads):
+                p.grad = g
+            opt.step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        # single-GPU reference on this rank's device: the same kernels, unsharded
+        ref = [torch.nn.Parameter(v.clone()) for v in vals]
+        for p in ref:
+            p.grad_dtype = None
+        cls = ZEEDENAdamW4Bit if recipe == "ze-eden" else ZIPSRAdamW4Bit
+        single = cls(ref, quant_rng_seed=9)
+        for step_grads in grads:
+            for p, g in zip(ref, step_grads):
+                p.grad = g
+            single.step()
+        torch.cuda.synchronize()
+        ok = all(torch.equal(a.detach().view(torch.int32), b.detach().view(torch.int32))
+                 for a, b in zip(params, ref))
+        q.put((rank, ok, None))
+    except Exception as e:  # report to the parent instead of hanging it
+        q.put((rank, False, repr(e)))
+    finally:
+        if dist.is_initialized():
+            dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("recipe,rounds", [("ze-eden", 1), ("ze-eden", 3), ("zip-sr", 2)])
+def test_zero1_two_gpus_matches_single_gpu_bit_exact(recipe, rounds):
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29600 + (os.getpid() % 500)
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, recipe, rounds, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    assert all(ok for _, ok, _ in results), results

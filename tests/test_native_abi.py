@@ -38,19 +38,21 @@ def test_library_loads_and_exports_every_declared_symbol():
 
 def test_struct_layouts_match_header():
     # sizes follow from the C declarations (natural alignment, x86-64)
-    assert ctypes.sizeof(N.Scheme) == 64 + 8 + N.LUT_BINS + 72 + 8 + 4
+    assert ctypes.sizeof(N.Scheme) == 64 + 12 + N.LUT_BINS + 72 + 8 + 4
     assert ctypes.sizeof(N.Hyper) == 48
     assert ctypes.sizeof(N.QTensor) == 88
     assert ctypes.sizeof(N.FTensor) == 48
 
 
 def _lut_search(s: N.Scheme, x: np.ndarray) -> np.ndarray:
-    """numpy copy of the kernels' table search: exact bin floor((x+1)*512)."""
-    lut = np.frombuffer(bytes(s.lut), dtype=np.uint8)
+    """numpy copy of the kernels' table search: exact bin floor((x+1)*bins/2)."""
+    nb = s.lut_bins
+    half = np.float32(nb // 2)
+    lut = np.frombuffer(bytes(s.lut), dtype=np.uint8)[:nb].astype(np.int64)
     thr = np.array(list(s.thr), dtype=np.float32)
-    b = np.floor(x.astype(np.float32) * np.float32(512.0)).astype(np.int64) + 512
-    last = int(lut[N.LUT_BINS - 1])
-    lut = np.append(lut.astype(np.int64), last + int(thr[last + 1] <= 1.0))   # edge x == 1
+    b = np.floor(x.astype(np.float32) * half).astype(np.int64) + nb // 2
+    last = int(lut[nb - 1])
+    lut = np.append(lut, last + int(thr[last + 1] <= 1.0))   # edge x == 1
     k = lut[b]
     return k + (x >= thr[k + 1]).astype(np.int64)
 
@@ -92,6 +94,13 @@ def test_scheme_tables_reproduce_the_reference_rounding_rule(scheme):
     np.testing.assert_array_equal(got, want)
 
 
+def test_bin_counts_are_the_coarsest_valid():
+    assert Q.prepared("nf4").lut_bins == 32
+    assert Q.prepared("dyn4_nz").lut_bins == 1024
+    for scheme in Q.SCHEMES:
+        assert Q.prepared(scheme).lut_bins in (32, 64, 128, 256, 512, 1024)
+
+
 def test_zero_state_matches_oracle_init():
     for scheme, eden in (("nf4", False), ("dyn4_nz", True), ("dyn4_upd_sr_fp32read", False),
                          ("nf4_sr", False)):
@@ -118,15 +127,15 @@ def test_step_entry_point_validates_before_touching_the_gpu():
     t = (N.QTensor * 1)(N.QTensor(16, 16, 4, 4, 4, 4, None, None, 100, 0, 0, 0))
     h = (N.Hyper * 1)(N.Hyper())
     s = Q.prepared("nf4")
-    rc = N.lib().aw4_step_quantized(s, Q.prepared("dyn4_nz"), 1, N.F32, N.F32, t, 1, h, 1, 0, None)
+    rc = N.lib().aw4_step_quantized(s, Q.prepared("dyn4_nz"), 1, N.F32, N.F32, t, 1, h, 1, 0, 0, None)
     assert rc == N.AW4_ERR_INVALID
     assert b"multiple of 128" in N.lib().aw4_last_error()
     rc = N.lib().aw4_step_quantized(Q.prepared("dyn4_upd_sr_fp32read"), s, 0, N.F32, N.F32, t, 1,
-                                    h, 1, 0, None)
+                                    h, 1, 0, 0, None)
     assert rc == N.AW4_ERR_UNSUPPORTED
     t[0].numel = 128
     t[0].hyper = 3
-    rc = N.lib().aw4_step_quantized(s, s, 0, N.F32, N.F32, t, 1, h, 1, 0, None)
+    rc = N.lib().aw4_step_quantized(s, s, 0, N.F32, N.F32, t, 1, h, 1, 0, 0, None)
     assert rc == N.AW4_ERR_INVALID and b"hyper index" in N.lib().aw4_last_error()
-    rc = N.lib().aw4_step_quantized(s, s, 0, N.BF16, N.F32, t, 1, h, 1, 0, None)
+    rc = N.lib().aw4_step_quantized(s, s, 0, N.BF16, N.F32, t, 1, h, 1, 0, 0, None)
     assert rc == N.AW4_ERR_UNSUPPORTED
