@@ -95,6 +95,7 @@ SIGNATURES = {
     "aw4_dequantize_blocks": ([ctypes.POINTER(Scheme), _VP, _VP, _I64, _VP, _I32, _VP], _I32),
     "aw4_pack_codes": ([_VP, _I64, _VP, _I32, _VP], _I32),
     "aw4_unpack_codes": ([_VP, _I64, _VP, _I32, _VP], _I32),
+    "aw4_selfcheck_math": ([_VP, _I32, _VP], _I32),
 }
 
 

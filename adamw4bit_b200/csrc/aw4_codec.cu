@@ -25,12 +25,13 @@ template <int MODE>
 __global__ void __launch_bounds__(kThreads)
 quantize_kernel(const __grid_constant__ aw4_scheme scheme, int eden, const float* x,
                 int64_t n_blocks, uint8_t* codes, float* scales, const float* draws,
-                uint64_t key, uint32_t step, uint32_t ordinal, float sr_bias, float sr_eps) {
+                uint64_t key, uint32_t step, uint32_t ordinal, float sr_bias, float sr_eps,
+                float one) {
     __shared__ __align__(16) SmemScheme S;
     __shared__ __align__(16) float scratch[kThreads / 32][kWarpScratch];
     load_scheme(S, scheme, threadIdx.x, kThreads);
     __syncthreads();
-    const GroupCtx g = group_ctx(scratch[threadIdx.x >> 5], threadIdx.x & 31);
+    const GroupCtx g = group_ctx(scratch[threadIdx.x >> 5], threadIdx.x & 31, one);
     const SchemeRegs R = scheme_regs(S, threadIdx.x & 31);
     const int group = threadIdx.x >> 4;
     const int64_t n_tiles = (n_blocks + kBlocksPerTile - 1) / kBlocksPerTile;
@@ -148,17 +149,18 @@ extern "C" int32_t aw4_quantize_blocks(const aw4_scheme* scheme, int32_t eden, c
     switch (scheme->round_mode) {
     case AW4_RTN:
         quantize_kernel<AW4_RTN><<<grid, kThreads, 0, s>>>(*scheme, eden, x, n_blocks, codes, scales,
-                                                           draws, key, step, ordinal, sr_bias, sr_eps);
+                                                           draws, key, step, ordinal, sr_bias, sr_eps,
+                                                           1.0f);
         break;
     case AW4_SR_VALUE:
         quantize_kernel<AW4_SR_VALUE><<<grid, kThreads, 0, s>>>(*scheme, eden, x, n_blocks, codes,
                                                                 scales, draws, key, step, ordinal,
-                                                                sr_bias, sr_eps);
+                                                                sr_bias, sr_eps, 1.0f);
         break;
     case AW4_SR_UPDATE:
         quantize_kernel<AW4_SR_UPDATE><<<grid, kThreads, 0, s>>>(*scheme, eden, x, n_blocks, codes,
                                                                  scales, draws, key, step, ordinal,
-                                                                 sr_bias, sr_eps);
+                                                                 sr_bias, sr_eps, 1.0f);
         break;
     default:
         return fail(AW4_ERR_INVALID, "aw4_quantize_blocks: bad round mode");

@@ -65,69 +65,162 @@ constexpr float kMarksteinMinNumerator = 0x1p-100f;
 constexpr float kMarksteinMaxDivisor = 0x1p26f;
 constexpr float kMarksteinMinDivisor = 0x1p-100f;
 
-// True if some value is a nonzero of magnitude below 2^-100 (it takes the
-// IEEE division path instead of div_markstein).
-__device__ __forceinline__ bool any_tiny(const float v[8]) {
-    bool t = false;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) t |= (fabsf(v[i]) < kMarksteinMinNumerator) & (v[i] != 0.0f);
-    return t;
+// ---------------------------------------------------------------------------
+// Reciprocal and square root from the hardware approximations, refined by
+// one Newton-Raphson step (reciprocal) and one Markstein correction (square
+// root): Markstein, IBM J. Res. Dev. 34(1), 1990; Muller et al., "Handbook of
+// Floating-Point Arithmetic", 2nd ed., ch. 4-5.  Both are verified
+// exhaustively against the IEEE round-to-nearest operations on the device
+// (aw4_selfcheck_math, every float32 of their domains) before the kernels rely
+// on them:
+//   rcp_nr(b)  == RN(1/b)     for every b with 2^-126 <= |b| <= 2^126
+//   sqrt_nr(x) == RN(sqrt(x)) for every x in [2^-102, 2^128) and x == 0
+// (below 2^-102 the remainder x - s^2 underflows and sqrt_nr is not exact;
+// the step only feeds it values scaled into range).
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float rcp_approx(float b) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(b));
+    return y;
+}
+__device__ __forceinline__ float rsqrt_approx(float x) {
+    float y;
+    asm("rsqrt.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+__device__ __forceinline__ float rcp_nr(float b) {
+    const float y = rcp_approx(b);
+    const float e = ffma(-b, y, 1.0f);   // 1 - b*y, exact to one rounding
+    return ffma(e, y, y);
+}
+constexpr float kNrMin = 0x1p-126f;
+// x == 0 gives +0: the approximation reads max(x, 2^-126), so y is finite
+// and every later product is a zero.
+__device__ __forceinline__ float sqrt_nr(float x) {
+    const float y = rsqrt_approx(fmaxf(x, kNrMin));
+    const float s = fmul(x, y);
+    const float h = fmul(0.5f, y);
+    const float r = ffma(-s, s, x);      // x - s^2, exact
+    return ffma(r, h, s);
 }
 
-// Packed float32 pairs (Blackwell f32x2, IEEE round-to-nearest).  Only FMA
-// and multiply are provided: ptxas may contract a packed multiply feeding a
-// packed add/sub into one FMA (even with explicit .rn), which would break
-// bit-exactness, so additions stay scalar and packed products must feed only
-// FMA operands, divisions or memory.
-__device__ __forceinline__ unsigned long long pk2(float lo, float hi) {
-    unsigned long long r;
+// Three-input max/min (Blackwell).  max3_nan propagates NaN like torch.max;
+// min3 ignores a NaN operand (its callers check finiteness separately).
+__device__ __forceinline__ float max3_nan(float a, float b, float c) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+__device__ __forceinline__ float min3(float a, float b, float c) {
+    float r;
+    asm("min.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+
+// Max of |v[i]| over a lane's 8 values (NaN-propagating, like torch.max).
+__device__ __forceinline__ float lane_absmax(const float v[8]) {
+    float a = max3_nan(fabsf(v[0]), fabsf(v[1]), fabsf(v[2]));
+    a = max3_nan(a, fabsf(v[3]), fabsf(v[4]));
+    a = max3_nan(a, fabsf(v[5]), fabsf(v[6]));
+    return max_nan(a, fabsf(v[7]));
+}
+// Min of |v[i]| over a lane's 8 values.
+__device__ __forceinline__ float lane_absmin(const float v[8]) {
+    float a = min3(fabsf(v[0]), fabsf(v[1]), fabsf(v[2]));
+    a = min3(a, fabsf(v[3]), fabsf(v[4]));
+    a = min3(a, fabsf(v[5]), fabsf(v[6]));
+    return fminf(a, fabsf(v[7]));
+}
+
+// True if some value is a nonzero of magnitude below 2^-100 (such a lane
+// takes the IEEE division path instead of div_markstein).  A lane whose
+// smallest magnitude is at least 2^-100 is decided by one compare; otherwise
+// (a zero, a tiny value or a NaN is present) the values are tested one by
+// one: 2|v| - 1 in the integer domain maps zeros to the top of the range.
+__device__ __forceinline__ bool any_tiny(const float v[8]) {
+    if (lane_absmin(v) >= kMarksteinMinNumerator) return false;
+    const uint32_t lim = 2u * (uint32_t)__float_as_int(kMarksteinMinNumerator) - 1u;
+    uint32_t m = 0xffffffffu;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m = min(m, 2u * (uint32_t)__float_as_int(v[i]) - 1u);
+    return m < lim;
+}
+
+// ---------------------------------------------------------------------------
+// Packed float32 pairs (Blackwell f32x2, IEEE round-to-nearest).
+// Only multiply and FMA are used.  ptxas may contract a packed multiply
+// feeding a packed add/sub into one FMA (even with explicit .rn), so an
+// addition is written as fma(a, one, b) with `one` a runtime 1.0 read from a
+// kernel parameter: the product a*one is exact, the sum is rounded once, and
+// no multiply can be fused into it.
+// ---------------------------------------------------------------------------
+typedef unsigned long long f2;
+__device__ __forceinline__ f2 pk2(float lo, float hi) {
+    f2 r;
     asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
     return r;
 }
-__device__ __forceinline__ void upk2(unsigned long long r, float& lo, float& hi) {
+__device__ __forceinline__ void upk2(f2 r, float& lo, float& hi) {
     asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
 }
-// d[i] = a[i] * b[i] for i in 0..7
+__device__ __forceinline__ f2 f2_mul(f2 a, f2 b) {
+    f2 r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+__device__ __forceinline__ f2 f2_fma(f2 a, f2 b, f2 c) {
+    f2 r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+// d[i] = a[i] * b[i]
 __device__ __forceinline__ void vmul8(float d[8], const float a[8], const float b[8]) {
 #pragma unroll
-    for (int i = 0; i < 8; i += 2) {
-        unsigned long long r;
-        asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(pk2(a[i], a[i + 1])), "l"(pk2(b[i], b[i + 1])));
-        upk2(r, d[i], d[i + 1]);
-    }
+    for (int i = 0; i < 8; i += 2)
+        upk2(f2_mul(pk2(a[i], a[i + 1]), pk2(b[i], b[i + 1])), d[i], d[i + 1]);
 }
 // d[i] = a[i] * s
 __device__ __forceinline__ void vmuls8(float d[8], const float a[8], float s) {
-    const unsigned long long ss = pk2(s, s);
+    const f2 ss = pk2(s, s);
 #pragma unroll
-    for (int i = 0; i < 8; i += 2) {
-        unsigned long long r;
-        asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(pk2(a[i], a[i + 1])), "l"(ss));
-        upk2(r, d[i], d[i + 1]);
-    }
+    for (int i = 0; i < 8; i += 2) upk2(f2_mul(pk2(a[i], a[i + 1]), ss), d[i], d[i + 1]);
+}
+// d[i] = fma(a[i], b[i], c[i])
+__device__ __forceinline__ void vfma8(float d[8], const float a[8], const float b[8],
+                                      const float c[8]) {
+#pragma unroll
+    for (int i = 0; i < 8; i += 2)
+        upk2(f2_fma(pk2(a[i], a[i + 1]), pk2(b[i], b[i + 1]), pk2(c[i], c[i + 1])), d[i], d[i + 1]);
 }
 // d[i] = fma(s, a[i], c[i])
 __device__ __forceinline__ void vfmas8(float d[8], float s, const float a[8], const float c[8]) {
-    const unsigned long long ss = pk2(s, s);
+    const f2 ss = pk2(s, s);
 #pragma unroll
-    for (int i = 0; i < 8; i += 2) {
-        unsigned long long r;
-        asm("fma.rn.f32x2 %0, %1, %2, %3;"
-            : "=l"(r) : "l"(ss), "l"(pk2(a[i], a[i + 1])), "l"(pk2(c[i], c[i + 1])));
-        upk2(r, d[i], d[i + 1]);
-    }
+    for (int i = 0; i < 8; i += 2)
+        upk2(f2_fma(ss, pk2(a[i], a[i + 1]), pk2(c[i], c[i + 1])), d[i], d[i + 1]);
+}
+// d[i] = fma(a[i], s, c): scalar multiplier and addend
+__device__ __forceinline__ void vfmass8(float d[8], const float a[8], float s, float c) {
+    const f2 ss = pk2(s, s), cc = pk2(c, c);
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) upk2(f2_fma(pk2(a[i], a[i + 1]), ss, cc), d[i], d[i + 1]);
+}
+// d[i] = RN(a[i] + b[i]), with one == 1.0 at run time
+__device__ __forceinline__ void vadd8(float d[8], const float a[8], const float b[8], float one) {
+    const f2 oo = pk2(one, one);
+#pragma unroll
+    for (int i = 0; i < 8; i += 2)
+        upk2(f2_fma(pk2(a[i], a[i + 1]), oo, pk2(b[i], b[i + 1])), d[i], d[i + 1]);
 }
 // q[i] = RN(a[i] / b) with y = RN(1 / b) (div_markstein, pairwise)
 __device__ __forceinline__ void vdiv_markstein8(float q[8], const float a[8], float b, float y) {
-    const unsigned long long bb = pk2(-b, -b), yy = pk2(y, y);
+    const f2 bb = pk2(-b, -b), yy = pk2(y, y);
 #pragma unroll
     for (int i = 0; i < 8; i += 2) {
-        const unsigned long long aa = pk2(a[i], a[i + 1]);
-        unsigned long long q0, r, q1;
-        asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(q0) : "l"(aa), "l"(yy));
-        asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(q0), "l"(bb), "l"(aa));
-        asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(q1) : "l"(r), "l"(yy), "l"(q0));
-        upk2(q1, q[i], q[i + 1]);
+        const f2 aa = pk2(a[i], a[i + 1]);
+        const f2 q0 = f2_mul(aa, yy);
+        const f2 r = f2_fma(q0, bb, aa);
+        upk2(f2_fma(r, yy, q0), q[i], q[i + 1]);
     }
 }
 

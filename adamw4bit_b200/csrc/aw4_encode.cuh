@@ -11,78 +11,103 @@
 
 namespace aw4 {
 
-// Per-warp scratch for EDEN sums and the update-SR level table.
-// EDEN: four tables (num/den x the warp's 2 groups) of 16 rows x 12 floats
-// (8 products + 4 pad).  The 12-float rows make each quarter-warp's float4
-// row writes hit 32 distinct banks; tables 200 floats apart start 8 banks
-// apart, so the 32 lanes' column reads hit 32 distinct banks too.
-constexpr int kEdenRow = 12;
-constexpr int kEdenTable = 200;
-constexpr int kWarpScratch = 4 * kEdenTable + 32 /* update-SR level tables */;
+// Per-warp scratch for EDEN sums and the update-SR level tables.
+//
+// EDEN products go to four column-major tables per warp (numerator and
+// denominator for each of the warp's two groups): 8 columns of 16 rows, with
+// a column stride of 20 floats.  A lane (row j) writes its 8 products to
+// address 20c + j: the two groups' tables start 16 banks apart, so the 32
+// lanes of each store hit 32 distinct banks.  A reading lane takes one whole
+// column as four float4 (rows 4k .. 4k+3); with the 20-float stride the 8
+// columns of a quarter-warp start in 8 distinct 4-bank groups.  Column totals
+// are then exchanged through 16 floats per group, interleaved as
+// (numerator, denominator) pairs.
+constexpr int kEdenCol = 20;                       // column stride (16 rows + 4 pad)
+constexpr int kEdenTable = 8 * kEdenCol;           // 160 floats
+// group h: numerator table at 336h, denominator table at 160 + 336h
+constexpr int kEdenDen = 160;                      // denominator table offset
+constexpr int kEdenGroup = 336;                    // second group's offset (16 mod 32)
+constexpr int kEdenTotals = 656;                   // 2 groups x 16 floats
+constexpr int kSrLevels = kEdenTotals + 32;        // 2 groups x 16 floats
+constexpr int kWarpScratch = kSrLevels + 32;       // 720 floats
+static_assert(kEdenGroup % 32 == 16 && kEdenDen % 32 == 0, "bank offsets");
+static_assert(kEdenDen >= kEdenTable && kEdenGroup >= kEdenDen + kEdenTable, "tables overlap");
+static_assert(kEdenTotals >= kEdenGroup + kEdenDen + kEdenTable && kEdenTotals % 4 == 0, "");
 
 struct GroupCtx {
-    float* eden_num;   // this group's products tables
-    float* eden_den;
+    float* tab_num;    // this group's column-major product tables
+    float* tab_den;
+    const float* rd;   // the column this lane reduces (numerator or denominator table)
+    float* totals;     // this group's 16 interleaved column totals
     float* levels;     // 16 floats: update-SR preconditioner of each level
     int j;             // lane within the group (0..15)
     int lane;          // lane within the warp
+    float one;         // 1.0 at run time (packed additions)
 };
 
-__device__ __forceinline__ GroupCtx group_ctx(float* warp_scratch, int lane) {
+__device__ __forceinline__ GroupCtx group_ctx(float* warp_scratch, int lane, float one) {
     const int h = lane >> 4;
     GroupCtx g;
-    g.eden_num = warp_scratch + (2 * h) * kEdenTable;
-    g.eden_den = warp_scratch + (2 * h + 1) * kEdenTable;
-    g.levels = warp_scratch + 4 * kEdenTable + 16 * h;
+    g.tab_num = warp_scratch + kEdenGroup * h;
+    g.tab_den = warp_scratch + kEdenDen + kEdenGroup * h;
     g.j = lane & 15;
+    g.rd = (g.j < 8 ? g.tab_num : g.tab_den) + kEdenCol * (g.j & 7);
+    g.totals = warp_scratch + kEdenTotals + 16 * h;
+    g.levels = warp_scratch + kSrLevels + 16 * h;
     g.lane = lane;
+    g.one = one;
     return g;
 }
 
-// Sum of the block's 128 products in torch's CPU reduction order for
-// (nb, 128).sum(dim=1): vector v (values 8v .. 8v+7) accumulates into
-// accumulator v % 4, the accumulators combine in order, then the 8 lanes are
-// summed in order from zero.  Lane j of the group holds vector v = j.
-// Returns (num, den) totals, valid in every lane of the group.
+// Sums of the block's 128 numerator and denominator products in torch's CPU
+// reduction order for (nb, 128).sum(dim=1): vector v (values 8v .. 8v+7)
+// accumulates into accumulator v % 4, the four accumulators combine in
+// order, then the 8 vector lanes are summed in order.  Lane j of the group
+// holds vector v = j.  The leading "0 +" of each chain is dropped: it can
+// only turn a -0 into +0, and the sums feed max(den, 1e-12) and a quotient
+// whose numerator is a sum of squares, so zero signs never reach a result.
+// Returns (num, den), valid in every lane of the group.
 __device__ __forceinline__ float2 eden_sums(const GroupCtx& g, const float np[8],
                                             const float dp[8]) {
-    float4* rn = reinterpret_cast<float4*>(g.eden_num + kEdenRow * g.j);
-    float4* rd = reinterpret_cast<float4*>(g.eden_den + kEdenRow * g.j);
-    rn[0] = make_float4(np[0], np[1], np[2], np[3]);
-    rn[1] = make_float4(np[4], np[5], np[6], np[7]);
-    rd[0] = make_float4(dp[0], dp[1], dp[2], dp[3]);
-    rd[1] = make_float4(dp[4], dp[5], dp[6], dp[7]);
-    __syncwarp();
-    // lanes 0-7: numerator column c; lanes 8-15: denominator column c
-    const float* tab = (g.j < 8) ? g.eden_num : g.eden_den;
-    const int c = g.j & 7;
-    float acc[4];
 #pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        float a = fadd(0.0f, tab[kEdenRow * k + c]);
-        a = fadd(a, tab[kEdenRow * (k + 4) + c]);
-        a = fadd(a, tab[kEdenRow * (k + 8) + c]);
-        a = fadd(a, tab[kEdenRow * (k + 12) + c]);
-        acc[k] = a;
+    for (int c = 0; c < 8; ++c) {
+        g.tab_num[kEdenCol * c + g.j] = np[c];
+        g.tab_den[kEdenCol * c + g.j] = dp[c];
     }
-    const float t = fadd(fadd(fadd(acc[0], acc[1]), acc[2]), acc[3]);
-    __syncwarp();  // tables are reused by the next block
-    // column totals in order from zero: each lane chains its half's 8 totals
-    const int base = g.lane & 24;   // group base + numerator/denominator half
-    float chain = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) chain = fadd(chain, __shfl_sync(0xffffffffu, t, base + i));
-    const float num = __shfl_sync(0xffffffffu, chain, g.lane & 16);
-    const float den = __shfl_sync(0xffffffffu, chain, (g.lane & 16) | 8);
+    __syncwarp();
+    // lanes 0-7: numerator column j; lanes 8-15: denominator column j - 8
+    const float4* col = reinterpret_cast<const float4*>(g.rd);
+    const float4 r0 = col[0], r1 = col[1], r2 = col[2], r3 = col[3];
+    const f2 oo = pk2(g.one, g.one);
+    // (acc0, acc1) over rows (0,1), (4,5), (8,9), (12,13); (acc2, acc3) likewise
+    f2 a01 = pk2(r0.x, r0.y), a23 = pk2(r0.z, r0.w);
+    a01 = f2_fma(pk2(r1.x, r1.y), oo, a01);
+    a23 = f2_fma(pk2(r1.z, r1.w), oo, a23);
+    a01 = f2_fma(pk2(r2.x, r2.y), oo, a01);
+    a23 = f2_fma(pk2(r2.z, r2.w), oo, a23);
+    a01 = f2_fma(pk2(r3.x, r3.y), oo, a01);
+    a23 = f2_fma(pk2(r3.z, r3.w), oo, a23);
+    float acc0, acc1, acc2, acc3;
+    upk2(a01, acc0, acc1);
+    upk2(a23, acc2, acc3);
+    const float t = fadd(fadd(fadd(acc0, acc1), acc2), acc3);
+    g.totals[2 * (g.j & 7) + (g.j >> 3)] = t;
+    __syncwarp();
+    const float4* tot = reinterpret_cast<const float4*>(g.totals);
+    const float4 t0 = tot[0], t1 = tot[1], t2 = tot[2], t3 = tot[3];
+    // (num, den) chained over the 8 columns in order
+    f2 ch = pk2(t0.x, t0.y);
+    ch = f2_fma(pk2(t0.z, t0.w), oo, ch);
+    ch = f2_fma(pk2(t1.x, t1.y), oo, ch);
+    ch = f2_fma(pk2(t1.z, t1.w), oo, ch);
+    ch = f2_fma(pk2(t2.x, t2.y), oo, ch);
+    ch = f2_fma(pk2(t2.z, t2.w), oo, ch);
+    ch = f2_fma(pk2(t3.x, t3.y), oo, ch);
+    ch = f2_fma(pk2(t3.z, t3.w), oo, ch);
+    __syncwarp();  // tables and totals are reused by the next block
+    float num, den;
+    upk2(ch, num, den);
     return make_float2(num, den);
-}
-
-// Max of |v[i]| over a lane's 8 values (NaN-propagating, like torch.max).
-__device__ __forceinline__ float lane_absmax(const float v[8]) {
-    float a = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) a = max_nan(a, fabsf(v[i]));
-    return a;
 }
 
 // Encodes the group's block.  v: this lane's 8 working values; amax: their
@@ -112,7 +137,7 @@ __device__ __forceinline__ uint32_t encode_block(const SmemScheme& S, const Sche
     if (fin) {
         const bool need_guard = (MODE != AW4_RTN) || eden;
         if (sc <= kMarksteinMaxDivisor && !(need_guard && any_tiny(v))) {
-            vdiv_markstein8(x, v, sc, frcp(sc));
+            vdiv_markstein8(x, v, sc, rcp_nr(sc));
         } else {
 #pragma unroll
             for (int i = 0; i < 8; ++i) x[i] = fdiv(v[i], sc);
@@ -156,7 +181,17 @@ __device__ __forceinline__ uint32_t encode_block(const SmemScheme& S, const Sche
         vmul8(np, x, x);
         vmul8(dp, x, q);
         const float2 nd = eden_sums(g, np, dp);
-        s = fmul(sc, fdiv(nd.x, max_nan(nd.y, kScaleFloor)));
+        // s' = s * (sum x^2 / max(sum x*q, 1e-12)); the divisor lies in
+        // [1e-12, 128] (|x| <= 1, |q| <= 1), so Markstein applies unless the
+        // numerator is a nonzero below 2^-100 or a sum is not finite (NaN
+        // fails every compare)
+        const float dd = max_nan(nd.y, kScaleFloor);
+        const float ratio = (dd <= kMarksteinMaxDivisor &&
+                             (nd.x == 0.0f ||
+                              (nd.x >= kMarksteinMinNumerator && nd.x <= 0x1p100f)))
+                                ? div_markstein(nd.x, dd, rcp_nr(dd))
+                                : fdiv(nd.x, dd);
+        s = fmul(sc, ratio);
     }
     *scale_out = s;
     uint32_t packed = 0;

@@ -20,6 +20,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 #include <cstdio>
 #include <cstring>
 #include <vector>
@@ -31,6 +32,8 @@ namespace aw4 {
 
 constexpr int kMaxTensors = 300;   // tensors per launch (kernel parameter space)
 constexpr int kMaxHypers = 8;      // distinct per-step scalar sets per launch
+constexpr int kSubBlocks = 2;      // blocks each 16-lane group takes per tile
+constexpr int kStepBlocksPerTile = kBlocksPerTile * kSubBlocks;   // 32 blocks = 4096 values
 
 struct KDesc {
     void* param;
@@ -48,11 +51,23 @@ struct KDesc {
     int32_t hyper;
 };
 
+// One hyper-parameter set as the kernel reads it: the caller's aw4_hyper plus
+// host-derived constants of the fast denominator/update path (fast_bounds).
+struct HyperDev {
+    float w1, w2, decay, neg_step;
+    float sqrt_bc2, eps, sr_bias, rcp_sqrt_bc2;   // rcp: RN(1 / sqrt_bc2)
+    float pos_step;                               // lr / bc1 = -neg_step
+    float bsc, rbsc;                              // sqrt_bc2 * 2^24 and RN(1 / bsc)
+    float m1_fast_max, m2_fast_max;               // lane bounds of the fast path (-1: off)
+    uint32_t step;
+    uint64_t m1_key, m2_key;
+};
+
 struct StepLaunch {
     aw4_scheme m1, m2;
-    aw4_hyper hyper[kMaxHypers];
-    float rcp_sqrt_bc2[kMaxHypers];   // RN(1 / sqrt_bc2), IEEE division on the host
-    int32_t n_tensors, n_tiles, eden, pad;
+    HyperDev hyper[kMaxHypers];
+    int32_t n_tensors, n_tiles, eden;
+    float one;                        // 1.0, read at run time (packed additions)
     KDesc t[kMaxTensors];
 };
 static_assert(sizeof(StepLaunch) <= 32000, "kernel parameter space");
@@ -61,7 +76,7 @@ struct StepSmem {
     SmemScheme s1, s2;
     float scratch[kThreads / 32][kWarpScratch];
 };
-// 16-byte table reads (s2), and float4 rows in each warp's EDEN scratch
+// 8-byte table entries (s2), and float4 columns in each warp's EDEN scratch
 static_assert(offsetof(StepSmem, s2) % 16 == 0, "");
 static_assert(offsetof(StepSmem, scratch) % 16 == 0 && (kWarpScratch * 4) % 16 == 0, "");
 
@@ -74,6 +89,62 @@ __device__ __forceinline__ int find_tensor(const StepLaunch& L, int tile) {
     return lo;
 }
 
+// The update q[i] = RN(RN(neg_step * m1[i]) / den[i]) with
+// den = RN(RN(RN(sqrt(m2)) / sqrt_bc2) + eps) (adamw.py:685, 743), for a lane
+// whose values pass the fast-path bounds:
+//  * sqrt: sqrt_nr on m2 * 2^48 (exact scaling; every nonzero m2 >= 2^-149
+//    lands at or above 2^-101, where sqrt_nr is exact), carried negated;
+//    m2 == 0 reads 2^-126, whose root vanishes against eps (fast_bounds);
+//  * / sqrt_bc2: Markstein against bsc = sqrt_bc2 * 2^24, which undoes the
+//    2^24 of the scaled root exactly;
+//  * / den: Markstein with ny = rcp_nr(-den) = RN(-1/den) and the positive
+//    numerator nt = pos_step * m1 = -t: q0 = nt*ny, r = nt + q0*den (exact),
+//    q = q0 + r*ny.  Written this way a zero numerator of either sign yields
+//    the IEEE zero of t/den.
+__device__ __forceinline__ void update_fast(float q[8], const float m1[8], const float m2[8],
+                                            const HyperDev& H, float one) {
+    const f2 k48 = pk2(-0x1p48f, -0x1p48f), kmin = pk2(-0x1p-126f, -0x1p-126f);
+    const f2 half = pk2(0.5f, 0.5f), nbsc = pk2(-H.bsc, -H.bsc), rb = pk2(H.rbsc, H.rbsc);
+    const f2 neg1 = pk2(-one, -one), eps = pk2(H.eps, H.eps), one2 = pk2(one, one);
+    const f2 ps = pk2(H.pos_step, H.pos_step);
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+        // N = -(m2 * 2^48 + 2^-126): the sum rounds back to m2 * 2^48 unless m2 == 0
+        const f2 N = f2_fma(pk2(m2[i], m2[i + 1]), k48, kmin);
+        float n0, n1;
+        upk2(N, n0, n1);
+        const f2 y = pk2(rsqrt_approx(-n0), rsqrt_approx(-n1));
+        const f2 ns = f2_mul(N, y);                        // -s
+        const f2 h = f2_mul(half, y);
+        const f2 nr = f2_fma(ns, ns, N);                   // s^2 - x = -r
+        const f2 nroot = f2_fma(nr, h, ns);                // -(s + r*h) = -RN(sqrt(x))
+        // nd = -RN(root / bsc)
+        const f2 q0 = f2_mul(nroot, rb);
+        const f2 r0 = f2_fma(q0, nbsc, nroot);
+        const f2 nd = f2_fma(r0, rb, q0);
+        const f2 den = f2_fma(nd, neg1, eps);              // RN(d + eps)
+        float d0, d1;
+        upk2(den, d0, d1);
+        const f2 y0 = pk2(rcp_approx(-d0), rcp_approx(-d1));
+        const f2 e = f2_fma(den, y0, one2);                // 1 - (-den) * y0
+        const f2 ny = f2_fma(e, y0, y0);                   // RN(-1 / den)
+        const f2 nt = f2_mul(pk2(m1[i], m1[i + 1]), ps);
+        const f2 qa = f2_mul(nt, ny);
+        const f2 rr = f2_fma(qa, den, nt);
+        upk2(f2_fma(rr, ny, qa), q[i], q[i + 1]);
+    }
+}
+
+// The same quantities by the IEEE operations, for lanes outside the bounds.
+__device__ __forceinline__ void update_ieee(float q[8], const float m1[8], const float m2[8],
+                                            const HyperDev& H) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float den = fadd(fdiv(fsqrt(m2[i]), H.sqrt_bc2), H.eps);
+        q[i] = fdiv(fmul(H.neg_step, m1[i]), den);
+    }
+}
+
 template <int PT, int GT, int M1, int M2>
 __global__ void __launch_bounds__(kThreads, 4)
 step_kernel(const __grid_constant__ StepLaunch L) {
@@ -84,7 +155,8 @@ step_kernel(const __grid_constant__ StepLaunch L) {
     __syncthreads();
 
     const int lane = tid & 31;
-    const GroupCtx g = group_ctx(sm.scratch[tid >> 5], lane);
+    const float one = L.one;
+    const GroupCtx g = group_ctx(sm.scratch[tid >> 5], lane, one);
     const SchemeRegs r1 = scheme_regs(sm.s1, lane), r2 = scheme_regs(sm.s2, lane);
     const int group = tid >> 4;
     const int zf2 = L.m2.zero_floor;
@@ -94,97 +166,87 @@ step_kernel(const __grid_constant__ StepLaunch L) {
     for (int tile = blockIdx.x; tile < L.n_tiles; tile += gridDim.x) {
         while (ti + 1 < L.n_tensors && L.t[ti + 1].tile_begin <= tile) ++ti;
         const KDesc& D = L.t[ti];
-        const aw4_hyper& H = L.hyper[D.hyper];
-        const int blk = (tile - D.tile_begin) * kBlocksPerTile + group;
-        const bool active = blk < D.nblocks;
-        const int64_t e0 = (int64_t)blk * kBlock + 8 * g.j;
+        const HyperDev& H = L.hyper[D.hyper];
+        const int blk0 = (tile - D.tile_begin) * kStepBlocksPerTile + group;
+#pragma unroll 1
+        for (int sb = 0; sb < kSubBlocks; ++sb) {
+            const int blk = blk0 + sb * kBlocksPerTile;
+            const bool active = blk < D.nblocks;
+            const int64_t e0 = (int64_t)blk * kBlock + 8 * g.j;
 
-        float p[8], gr[8], m1[8], m2[8];
-        uint32_t w1 = 0, w2 = 0;
-        float s1 = 0.0f, s2 = 0.0f;
-        if (active) {
-            Elem<PT>::load8(D.param, e0, p);
-            Elem<GT>::load8(D.grad, e0, gr);
-            w1 = __ldcs(reinterpret_cast<const unsigned int*>(D.c1 + (e0 >> 1)));
-            w2 = __ldcs(reinterpret_cast<const unsigned int*>(D.c2 + (e0 >> 1)));
-            s1 = __ldcs(D.s1 + blk);
-            s2 = __ldcs(D.s2 + blk);
-        } else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) p[i] = gr[i] = 0.0f;
-        }
-        // Packed f32x2 ops are used only where operand fusion cannot change a
-        // result (FMA, and products consumed by an FMA, a division or a store):
-        // ptxas may contract a packed mul.rn feeding a packed add/sub.rn into
-        // one FMA, so every multiply -> add/sub chain below stays scalar.
-        // decode (quantization.py:996-999)
-        float d[8], t[8];
-        decode8(r1.cbv, w1, s1, m1);
-        decode8(r2.cbv, w2, s2, m2);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) d[i] = fsub(gr[i], m1[i]);
-        vfmas8(m1, H.w1, d, m1);                 // m1.lerp_(g, 1-b1)  (adamw.py:557)
-#pragma unroll
-        for (int i = 0; i < 8; ++i) d[i] = fsub(fmul(gr[i], gr[i]), m2[i]);
-        vfmas8(m2, H.w2, d, m2);                 // m2.lerp_(g*g, 1-b2) (adamw.py:684)
-        const float amax2 = lane_absmax(m2);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) t[i] = fsqrt(m2[i]);
-        // den = sqrt(m2) / sqrt(bc2) + eps (adamw.py:685); sqrt of a finite
-        // float is 0 or >= 2^-75, so Markstein's preconditions hold
-        if (is_finite(amax2) && H.sqrt_bc2 >= kMarksteinMinDivisor &&
-            H.sqrt_bc2 <= kMarksteinMaxDivisor) {
-            vdiv_markstein8(d, t, H.sqrt_bc2, L.rcp_sqrt_bc2[D.hyper]);
-        } else {
-#pragma unroll
-            for (int i = 0; i < 8; ++i) d[i] = fdiv(t[i], H.sqrt_bc2);
-        }
-        vmuls8(t, m1, H.neg_step);               // (-lr/bc1) * m1, consumed by a division
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-            const float den = fadd(d[i], H.eps);
-            const float pd = Elem<PT>::round(fmul(p[i], H.decay));   // p.mul_(1 - lr*wd)
-            p[i] = fadd(pd, fdiv(t[i], den));                       // p.addcdiv_(m1, den, -lr/bc1)
-        }
-        if (active) Elem<PT>::store8(D.param, e0, p);
-
-        // re-encode m1 (adamw.py:764-771)
-        float u[8];
-        if (M1 != AW4_RTN) {
-            if (D.d1 != nullptr && active) {
-                const float4* q = reinterpret_cast<const float4*>(D.d1 + e0);
-                const float4 a = __ldcs(q), b = __ldcs(q + 1);
-                u[0] = a.x; u[1] = a.y; u[2] = a.z; u[3] = a.w;
-                u[4] = b.x; u[5] = b.y; u[6] = b.z; u[7] = b.w;
+            float p[8], gr[8], m1[8], m2[8];
+            uint32_t w1 = 0, w2 = 0;
+            float s1 = 0.0f, s2 = 0.0f;
+            if (active) {
+                Elem<PT>::load8(D.param, e0, p);
+                Elem<GT>::load8(D.grad, e0, gr);
+                w1 = __ldcs(reinterpret_cast<const unsigned int*>(D.c1 + (e0 >> 1)));
+                w2 = __ldcs(reinterpret_cast<const unsigned int*>(D.c2 + (e0 >> 1)));
+                s1 = __ldcs(D.s1 + blk);
+                s2 = __ldcs(D.s2 + blk);
             } else {
-                philox_uniform8(H.m1_key, H.step, D.ordinal, (uint64_t)(D.elem_offset + e0), u);
+#pragma unroll
+                for (int i = 0; i < 8; ++i) p[i] = gr[i] = 0.0f;
             }
-        }
-        float ns1;
-        const uint32_t c1 =
-            encode_block<M1>(sm.s1, r1, g, m1, lane_absmax(m1), u, 0, 0, H.sr_bias, H.eps, &ns1);
+            // Packed f32x2 arithmetic throughout: multiplies, FMAs, and
+            // additions as fma(a, one, b) (no multiply can be fused into them).
+            // decode (quantization.py:996-999)
+            float d[8], q[8];
+            decode8(r1.cbv, w1, s1, m1);
+            decode8(r2.cbv, w2, s2, m2);
+            vfmas8(d, -one, m1, gr);                 // g - m1
+            vfmas8(m1, H.w1, d, m1);                 // m1.lerp_(g, 1-b1)  (adamw.py:557)
+            vmul8(q, gr, gr);                        // g*g
+            vfmas8(d, -one, m2, q);                  // g*g - m2
+            vfmas8(m2, H.w2, d, m2);                 // m2.lerp_(g*g, 1-b2) (adamw.py:684)
+            const float amax1 = lane_absmax(m1), amax2 = lane_absmax(m2);
 
-        // re-encode m2 (adamw.py:675-683 update-SR, 795-803 RTN + floor + EDEN)
-        if (M2 != AW4_RTN) {
-            if (D.d2 != nullptr && active) {
-                const float4* q = reinterpret_cast<const float4*>(D.d2 + e0);
-                const float4 a = __ldcs(q), b = __ldcs(q + 1);
-                u[0] = a.x; u[1] = a.y; u[2] = a.z; u[3] = a.w;
-                u[4] = b.x; u[5] = b.y; u[6] = b.z; u[7] = b.w;
+            // q = (-lr/bc1 * m1) / (sqrt(m2) / sqrt(bc2) + eps)  (adamw.py:685, 743)
+            float nt[8];
+            vmuls8(nt, m1, H.pos_step);
+            if (amax1 <= H.m1_fast_max && amax2 <= H.m2_fast_max && !any_tiny(nt)) {
+                update_fast(q, m1, m2, H, one);
             } else {
-                philox_uniform8(H.m2_key, H.step, D.ordinal, (uint64_t)(D.elem_offset + e0), u);
+                update_ieee(q, m1, m2, H);
             }
-        }
-        float ns2;
-        const uint32_t c2 =
-            encode_block<M2>(sm.s2, r2, g, m2, amax2, u, zf2, L.eden, H.sr_bias, H.eps, &ns2);
+            vmuls8(p, p, H.decay);                   // p.mul_(1 - lr*wd)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) p[i] = Elem<PT>::round(p[i]);
+            vadd8(p, q, p, one);                     // p.addcdiv_(m1, den, -lr/bc1)
+            if (active) Elem<PT>::store8(D.param, e0, p);
 
-        if (active) {
-            __stcs(reinterpret_cast<unsigned int*>(D.c1 + (e0 >> 1)), c1);
-            __stcs(reinterpret_cast<unsigned int*>(D.c2 + (e0 >> 1)), c2);
-            if (g.j == 0) {
-                __stcs(D.s1 + blk, ns1);
-                __stcs(D.s2 + blk, ns2);
+            // re-encode m1 (adamw.py:764-771)
+            float u[8];
+            if (M1 != AW4_RTN) {
+                if (D.d1 != nullptr && active) {
+                    Elem<AW4_F32>::load8(D.d1, e0, u);
+                } else {
+                    philox_uniform8(H.m1_key, H.step, D.ordinal, (uint64_t)(D.elem_offset + e0), u);
+                }
+            }
+            float ns1;
+            const uint32_t c1 =
+                encode_block<M1>(sm.s1, r1, g, m1, amax1, u, 0, 0, H.sr_bias, H.eps, &ns1);
+
+            // re-encode m2 (adamw.py:675-683 update-SR, 795-803 RTN + floor + EDEN)
+            if (M2 != AW4_RTN) {
+                if (D.d2 != nullptr && active) {
+                    Elem<AW4_F32>::load8(D.d2, e0, u);
+                } else {
+                    philox_uniform8(H.m2_key, H.step, D.ordinal, (uint64_t)(D.elem_offset + e0), u);
+                }
+            }
+            float ns2;
+            const uint32_t c2 =
+                encode_block<M2>(sm.s2, r2, g, m2, amax2, u, zf2, L.eden, H.sr_bias, H.eps, &ns2);
+
+            if (active) {
+                __stcs(reinterpret_cast<unsigned int*>(D.c1 + (e0 >> 1)), c1);
+                __stcs(reinterpret_cast<unsigned int*>(D.c2 + (e0 >> 1)), c2);
+                if (g.j == 0) {
+                    __stcs(D.s1 + blk, ns1);
+                    __stcs(D.s2 + blk, ns2);
+                }
             }
         }
     }
@@ -289,6 +351,56 @@ static int dtype_bytes(int dt) { return dt == AW4_F32 ? 4 : 2; }
 
 static bool aligned(const void* p, uintptr_t a) { return ((uintptr_t)p % a) == 0; }
 
+// A hyper-parameter set with the constants and lane bounds of update_fast.
+// The fast path needs (every bound below is checked per lane in the kernel):
+//  * eps in [2^-100, 2^25]: den = d + eps is normal and, with d <= 2^24, at
+//    most 2^26 (Markstein's divisor range);
+//  * sqrt_bc2 in [2^-76, 1]: bsc = sqrt_bc2 * 2^24 lies in Markstein's
+//    divisor range;
+//  * m2 in [0, 2^48 * bc2]: the scaled root stays finite and d <= 2^24; m2 is
+//    non-negative when the m2 codebook is and 0 <= w2 <= 1 (the lerp is then a
+//    convex combination under rounding);
+//  * m2 == 0 reads 2^-126 in the scaled domain, so d = RN(2^-87 / sqrt_bc2)
+//    instead of 0; that must stay below half an ulp of eps, so den == eps
+//    exactly as with d == 0;
+//  * |m1| <= 2^120 * min(eps, 1) / pos_step: nt and the quotient stay finite;
+//  * every nt is zero or of magnitude >= 2^-100 (checked in the kernel).
+static HyperDev hyper_dev(const aw4_hyper& h, const aw4_scheme& m2s) {
+    HyperDev d;
+    std::memset(&d, 0, sizeof(d));
+    d.w1 = h.w1;
+    d.w2 = h.w2;
+    d.decay = h.decay;
+    d.neg_step = h.neg_step;
+    d.sqrt_bc2 = h.sqrt_bc2;
+    d.eps = h.eps;
+    d.sr_bias = h.sr_bias;
+    d.step = h.step;
+    d.m1_key = h.m1_key;
+    d.m2_key = h.m2_key;
+    d.pos_step = -h.neg_step;
+    d.bsc = h.sqrt_bc2 * 0x1p24f;
+    // float32 divisions on the host (SSE): correctly rounded
+    volatile float one = 1.0f;
+    d.rcp_sqrt_bc2 = one / h.sqrt_bc2;
+    d.rbsc = one / d.bsc;
+    d.m1_fast_max = -1.0f;   // off: no lane passes
+    d.m2_fast_max = -1.0f;
+    float cb_min = m2s.codebook[0];
+    for (int k = 1; k < 16; ++k) cb_min = std::min(cb_min, m2s.codebook[k]);
+    const double eps = h.eps, sb = h.sqrt_bc2, ps = d.pos_step;
+    const bool ok = cb_min >= 0.0f && h.w2 >= 0.0f && h.w2 <= 1.0f && eps >= 0x1p-100 &&
+                    eps <= 0x1p25 && sb >= 0x1p-76 && sb <= 1.0 && ps >= 0.0 &&
+                    ps <= 3.0e38;
+    if (!ok) return d;
+    const double ulp_eps = (double)std::nextafter(h.eps, INFINITY) - eps;
+    if (!(0x1p-87 / sb * (1.0 + 0x1p-20) < 0.5 * ulp_eps)) return d;
+    d.m2_fast_max = (float)(0x1p48 * sb * sb * (1.0 - 0x1p-20));
+    const double m1max = 0x1p120 * std::min(eps, 1.0) / std::max(ps, 1e-300);
+    d.m1_fast_max = (float)std::min(m1max, 3.0e38);
+    return d;
+}
+
 // Grid: a multiple of the SM count, at most the resident CTAs, at most the work.
 template <typename Fn>
 static int grid_for(Fn fn, int device, int work) {
@@ -352,7 +464,7 @@ extern "C" int32_t aw4_step_quantized(const aw4_scheme* m1, const aw4_scheme* m2
     L->m1 = *m1;
     L->m2 = *m2;
     L->eden = eden ? 1 : 0;
-    int hmap[64];
+    L->one = 1.0f;
     int i = 0;
     int32_t rc = AW4_OK;
     while (i < n_tensors && rc == AW4_OK) {
@@ -374,12 +486,8 @@ extern "C" int32_t aw4_step_quantized(const aw4_scheme* m1, const aw4_scheme* m2
                 if (nh == kMaxHypers) break;
                 h = nh++;
                 hsrc.push_back(t.hyper);
-                L->hyper[h] = hypers[t.hyper];
-                // IEEE float32 division (SSE on the host): correctly rounded
-                volatile float one = 1.0f;
-                L->rcp_sqrt_bc2[h] = one / hypers[t.hyper].sqrt_bc2;
+                L->hyper[h] = hyper_dev(hypers[t.hyper], *m2);
             }
-            (void)hmap;
             KDesc& d = L->t[L->n_tensors++];
             d.param = t.param;
             d.grad = t.grad;
@@ -394,7 +502,7 @@ extern "C" int32_t aw4_step_quantized(const aw4_scheme* m1, const aw4_scheme* m2
             d.tile_begin = L->n_tiles;
             d.ordinal = t.ordinal;
             d.hyper = h;
-            const int64_t tiles = (d.nblocks + kBlocksPerTile - 1) / kBlocksPerTile;
+            const int64_t tiles = (d.nblocks + kStepBlocksPerTile - 1) / kStepBlocksPerTile;
             if ((int64_t)L->n_tiles + tiles > 0x7fffffffLL) {
                 rc = fail(AW4_ERR_INVALID, "launch exceeds 2^31 tiles");
                 break;

@@ -167,6 +167,14 @@ int32_t aw4_pack_codes(const uint8_t* codes, int64_t numel, uint8_t* packed,
 int32_t aw4_unpack_codes(const uint8_t* packed, int64_t numel, uint8_t* codes,
                          int32_t device, void* stream);
 
+/* Exhaustive device check of the reciprocal and square root the step kernel
+ * builds from the hardware approximations, against IEEE round-to-nearest, over
+ * every float32 of their domains (about 4e9 inputs each, a few ms).
+ * counts: device pointer to 2 uint64, zeroed here, receiving the mismatch
+ * counts [reciprocal, square root].  No reference counterpart: it validates
+ * this build's arithmetic on the running GPU. */
+int32_t aw4_selfcheck_math(uint64_t* counts, int32_t device, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
