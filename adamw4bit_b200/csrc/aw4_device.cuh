@@ -146,6 +146,21 @@ __device__ __forceinline__ bool any_tiny(const float v[8]) {
     return m < lim;
 }
 
+// Branch-free form of any_tiny, for warp votes: the lane minimum decides
+// most lanes; the exact per-value test is evaluated only when some lane of
+// the warp needs it (the vote keeps that branch uniform).
+__device__ __forceinline__ bool none_tiny_warp(const float v[8], bool lane_ok) {
+    bool ok = lane_ok && lane_absmin(v) >= kMarksteinMinNumerator;
+    if (!__all_sync(0xffffffffu, ok)) {
+        const uint32_t lim = 2u * (uint32_t)__float_as_int(kMarksteinMinNumerator) - 1u;
+        uint32_t m = 0xffffffffu;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) m = min(m, 2u * (uint32_t)__float_as_int(v[i]) - 1u);
+        ok = lane_ok && m >= lim;
+    }
+    return ok;
+}
+
 // ---------------------------------------------------------------------------
 // Packed float32 pairs (Blackwell f32x2, IEEE round-to-nearest).
 // Only multiply and FMA are used.  ptxas may contract a packed multiply

@@ -200,4 +200,57 @@ __device__ __forceinline__ uint32_t encode_block(const SmemScheme& S, const Sche
     return packed;
 }
 
+// encode_block for a warp whose blocks all meet the fast preconditions (the
+// caller has voted): a finite scale sc = max(absmax, 1e-12) <= 2^26, and, for
+// SR or EDEN, no nonzero value below 2^-100.  The same results as
+// encode_block, without its per-lane branches.
+template <int MODE>
+__device__ __forceinline__ uint32_t encode_fast(const SmemScheme& S, const SchemeRegs& R,
+                                                const GroupCtx& g, const float v[8], float sc,
+                                                const float u[8], int zero_floor, int eden,
+                                                float sr_bias, float sr_eps, float* scale_out) {
+    if (MODE == AW4_SR_UPDATE) {
+        g.levels[g.j] = precond(sc, S.cb[g.j], sr_bias, sr_eps);
+        __syncwarp();
+    }
+    float x[8];
+    int code[8];
+    vdiv_markstein8(x, v, sc, rcp_nr(sc));
+    const int floor_code = (MODE != AW4_RTN && zero_floor) ? 1 : 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const int idx = lut_search(S, R, x[i]);
+        if (MODE == AW4_RTN) {
+            code[i] = idx;  // the dyn4_nz floor is folded into the RTN table
+        } else {
+            code[i] = (MODE == AW4_SR_VALUE)
+                          ? value_sr_from_index(S.cb, idx, x[i], u[i])
+                          : update_sr_from_index(S.cb, g.levels, idx, x[i], sc, sr_bias, sr_eps,
+                                                 u[i]);
+            code[i] = max(code[i], floor_code);
+        }
+    }
+    if (MODE == AW4_SR_UPDATE) __syncwarp();  // level table reused by the next block
+    float s = sc;
+    if (eden) {
+        float q[8], np[8], dp[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) q[i] = level_of(R.cbv, code[i]);
+        vmul8(np, x, x);
+        vmul8(dp, x, q);
+        const float2 nd = eden_sums(g, np, dp);
+        // finite sums here: the divisor lies in [1e-12, 128]
+        const float dd = max_nan(nd.y, kScaleFloor);
+        const bool ok = nd.x == 0.0f || nd.x >= kMarksteinMinNumerator;
+        const float ratio = __all_sync(0xffffffffu, ok) ? div_markstein(nd.x, dd, rcp_nr(dd))
+                                                        : fdiv(nd.x, dd);
+        s = fmul(sc, ratio);
+    }
+    *scale_out = s;
+    uint32_t packed = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) packed |= (uint32_t)code[i] << (4 * i);
+    return packed;
+}
+
 }  // namespace aw4

@@ -145,6 +145,18 @@ __device__ __forceinline__ void update_ieee(float q[8], const float m1[8], const
     }
 }
 
+// SR uniforms of 8 values: the test-hook draws buffer when given, else the
+// in-kernel Philox stream of the moment.
+__device__ __forceinline__ void load_uniforms(float u[8], const float* draws, uint64_t key,
+                                              const HyperDev& H, const KDesc& D, int64_t e0,
+                                              bool active) {
+    if (draws != nullptr && active) {
+        Elem<AW4_F32>::load8(draws, e0, u);
+    } else {
+        philox_uniform8(key, H.step, D.ordinal, (uint64_t)(D.elem_offset + e0), u);
+    }
+}
+
 template <int PT, int GT, int M1, int M2>
 __global__ void __launch_bounds__(kThreads, 4)
 step_kernel(const __grid_constant__ StepLaunch L) {
@@ -200,10 +212,43 @@ step_kernel(const __grid_constant__ StepLaunch L) {
             vfmas8(d, -one, m2, q);                  // g*g - m2
             vfmas8(m2, H.w2, d, m2);                 // m2.lerp_(g*g, 1-b2) (adamw.py:684)
             const float amax1 = lane_absmax(m1), amax2 = lane_absmax(m2);
-
-            // q = (-lr/bc1 * m1) / (sqrt(m2) / sqrt(bc2) + eps)  (adamw.py:685, 743)
             float nt[8];
             vmuls8(nt, m1, H.pos_step);
+
+            // One warp-uniform decision per sub-block: when every lane meets the
+            // fast preconditions the rest runs without per-lane branches.
+            const float sc1 = max_nan(group_max16(amax1), kScaleFloor);
+            const float sc2 = max_nan(group_max16(amax2), kScaleFloor);
+            bool ok = active && amax1 <= H.m1_fast_max && amax2 <= H.m2_fast_max &&
+                      sc1 <= kMarksteinMaxDivisor && sc2 <= kMarksteinMaxDivisor;
+            ok = none_tiny_warp(nt, ok);
+            if (M1 != AW4_RTN) ok = none_tiny_warp(m1, ok);
+            if (M2 != AW4_RTN || L.eden) ok = none_tiny_warp(m2, ok);
+            float u[8];
+            if (__all_sync(0xffffffffu, ok)) {
+                update_fast(q, m1, m2, H, one);
+                vmuls8(p, p, H.decay);               // p.mul_(1 - lr*wd)
+#pragma unroll
+                for (int i = 0; i < 8; ++i) p[i] = Elem<PT>::round(p[i]);
+                vadd8(p, q, p, one);                 // p.addcdiv_(m1, den, -lr/bc1)
+                Elem<PT>::store8(D.param, e0, p);
+                if (M1 != AW4_RTN) load_uniforms(u, D.d1, H.m1_key, H, D, e0, true);
+                float ns1, ns2;
+                const uint32_t c1 =
+                    encode_fast<M1>(sm.s1, r1, g, m1, sc1, u, 0, 0, H.sr_bias, H.eps, &ns1);
+                if (M2 != AW4_RTN) load_uniforms(u, D.d2, H.m2_key, H, D, e0, true);
+                const uint32_t c2 =
+                    encode_fast<M2>(sm.s2, r2, g, m2, sc2, u, zf2, L.eden, H.sr_bias, H.eps, &ns2);
+                __stcs(reinterpret_cast<unsigned int*>(D.c1 + (e0 >> 1)), c1);
+                __stcs(reinterpret_cast<unsigned int*>(D.c2 + (e0 >> 1)), c2);
+                if (g.j == 0) {
+                    __stcs(D.s1 + blk, ns1);
+                    __stcs(D.s2 + blk, ns2);
+                }
+                continue;
+            }
+
+            // general path: per-lane guards, IEEE fallbacks, inactive groups
             if (amax1 <= H.m1_fast_max && amax2 <= H.m2_fast_max && !any_tiny(nt)) {
                 update_fast(q, m1, m2, H, one);
             } else {
@@ -216,26 +261,13 @@ step_kernel(const __grid_constant__ StepLaunch L) {
             if (active) Elem<PT>::store8(D.param, e0, p);
 
             // re-encode m1 (adamw.py:764-771)
-            float u[8];
-            if (M1 != AW4_RTN) {
-                if (D.d1 != nullptr && active) {
-                    Elem<AW4_F32>::load8(D.d1, e0, u);
-                } else {
-                    philox_uniform8(H.m1_key, H.step, D.ordinal, (uint64_t)(D.elem_offset + e0), u);
-                }
-            }
+            if (M1 != AW4_RTN) load_uniforms(u, D.d1, H.m1_key, H, D, e0, active);
             float ns1;
             const uint32_t c1 =
                 encode_block<M1>(sm.s1, r1, g, m1, amax1, u, 0, 0, H.sr_bias, H.eps, &ns1);
 
             // re-encode m2 (adamw.py:675-683 update-SR, 795-803 RTN + floor + EDEN)
-            if (M2 != AW4_RTN) {
-                if (D.d2 != nullptr && active) {
-                    Elem<AW4_F32>::load8(D.d2, e0, u);
-                } else {
-                    philox_uniform8(H.m2_key, H.step, D.ordinal, (uint64_t)(D.elem_offset + e0), u);
-                }
-            }
+            if (M2 != AW4_RTN) load_uniforms(u, D.d2, H.m2_key, H, D, e0, active);
             float ns2;
             const uint32_t c2 =
                 encode_block<M2>(sm.s2, r2, g, m2, amax2, u, zf2, L.eden, H.sr_bias, H.eps, &ns2);
