@@ -416,12 +416,14 @@ __device__ __forceinline__ void load_scheme(SmemScheme& s, const aw4_scheme& g, 
 
 // Per-lane register copies of a scheme's search constants and codebook level.
 struct SchemeRegs {
-    float cbv;    // cb[lane % 16], read by shuffles
-    float half;   // lut_bins / 2
-    float bias;   // 2^23 + lut_bins / 2
+    float cbv;             // cb[lane % 16], read by shuffles
+    float half;            // lut_bins / 2
+    float bias;            // 2^23 + lut_bins / 2
+    uint32_t tab_biased;   // shared address of tab, minus 0x4B000000 * 8 (mod 2^32)
 };
 __device__ __forceinline__ SchemeRegs scheme_regs(const SmemScheme& s, int lane) {
-    return SchemeRegs{s.cb[lane & 15], s.half_bins, s.bias};
+    const uint32_t tab = static_cast<uint32_t>(__cvta_generic_to_shared(&s.tab[0]));
+    return SchemeRegs{s.cb[lane & 15], s.half_bins, s.bias, tab - 0x4B000000u * 8u};
 }
 
 // Table search of a finite normalised value x in [-1, 1]: the stored code
@@ -431,9 +433,17 @@ __device__ __forceinline__ SchemeRegs scheme_regs(const SmemScheme& s, int lane)
 // product is exact, the sum lies in [2^23, 2^23 + N] where float32 spacing is
 // 1, and truncation of a positive value is its floor).
 __device__ __forceinline__ int lut_search(const SmemScheme& s, const SchemeRegs& r, float x) {
-    const int b = __float_as_int(__fmaf_rz(x, r.half, r.bias)) - 0x4B000000;
-    const float2 e = *reinterpret_cast<const float2*>(&s.tab[b]);
-    return __float_as_int(e.y) + (x >= e.x ? 1 : 0);
+    // entry address = bits * 8 + (table - 0x4B000000 * 8): the exponent bias
+    // of the bin index folds into the table base (32-bit shared address)
+    const uint32_t bits = __float_as_uint(__fmaf_rz(x, r.half, r.bias));
+    const uint32_t addr = bits * 8u + r.tab_biased;
+    float next;
+    int count;
+    asm("ld.shared.v2.b32 {%0, %1}, [%2];" : "=f"(next), "=r"(count) : "r"(addr));
+    int ge;   // -1 if x >= next, else 0
+    asm("set.ge.s32.f32 %0, %1, %2;" : "=r"(ge) : "f"(x), "f"(next));
+    (void)s;
+    return count - ge;
 }
 
 // Level of a code from the codebook held in registers: lane l keeps
@@ -510,13 +520,14 @@ __device__ __forceinline__ int update_sr_from_index(const float* cb, const float
     return (u < p) ? l : r;
 }
 
-// Max over the 16 lanes of a block group (lanes 16h .. 16h+15 of a warp).
+// Max over the 16 lanes of a block group (lanes 16h .. 16h+15 of a warp):
+// one warp reduction (Blackwell redux.f32) per group, NaN-propagating like
+// torch.max.
 __device__ __forceinline__ float group_max16(float v) {
-    v = max_nan(v, __shfl_xor_sync(0xffffffffu, v, 8));
-    v = max_nan(v, __shfl_xor_sync(0xffffffffu, v, 4));
-    v = max_nan(v, __shfl_xor_sync(0xffffffffu, v, 2));
-    v = max_nan(v, __shfl_xor_sync(0xffffffffu, v, 1));
-    return v;
+    const unsigned mask = (threadIdx.x & 16) ? 0xFFFF0000u : 0x0000FFFFu;
+    float r;
+    asm volatile("redux.sync.max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(v), "r"(mask));
+    return r;
 }
 
 }  // namespace aw4

@@ -196,7 +196,7 @@ __device__ __forceinline__ uint32_t encode_block(const SmemScheme& S, const Sche
     *scale_out = s;
     uint32_t packed = 0;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) packed |= (uint32_t)code[i] << (4 * i);
+    for (int i = 0; i < 8; ++i) packed += (uint32_t)code[i] << (4 * i);   // disjoint nibbles
     return packed;
 }
 
@@ -249,7 +249,7 @@ __device__ __forceinline__ uint32_t encode_fast(const SmemScheme& S, const Schem
     *scale_out = s;
     uint32_t packed = 0;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) packed |= (uint32_t)code[i] << (4 * i);
+    for (int i = 0; i < 8; ++i) packed += (uint32_t)code[i] << (4 * i);   // disjoint nibbles
     return packed;
 }
 

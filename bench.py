@@ -16,7 +16,9 @@ is far larger than L2, so no flush is needed between steps); ``e2e`` is the
 same metric through the public API with the gradients copied in from pinned
 host memory and the updated parameters copied back each step.
 ``--impl reference`` times the CPU oracle port of the reference algorithm on
-the host's cores on a bounded sample of the same workload.
+the host's cores on a bounded sample of the same workload.  ``--impl
+reference-gpu`` (and ``reference-gpu-eager``) time the reference's own CUDA
+path from the offline install under baseline/_ref, for comparison only.
 """
 
 from __future__ import annotations
@@ -206,6 +208,55 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_reference_gpu(args, rank, eager: bool):
+    """The reference's own CUDA path on this GPU (the "GPU bar"): its
+    ZEEDENAdamW4Bit with optimized=True (torch.compile per 512 Ki chunk) or,
+    with ``eager``, its eager path, on the same workload.  Imported from the
+    offline install under baseline/_ref; not part of the product."""
+    if rank != 0:
+        return
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    impl = "reference-gpu-eager" if eager else "reference-gpu"
+    if not os.path.isdir(os.path.join(ref, "adamw4bit")):
+        print(json.dumps({"impl": impl, "unavailable": "baseline/_ref is not installed"}))
+        return
+    sys.path.insert(0, ref)
+    from adamw4bit import ZEEDENAdamW4Bit as RefZE
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    shapes = llama3_8b_shapes()
+    if args.layers is not None:
+        shapes = shapes[:1 + 9 * args.layers] + shapes[-2:]
+    if args.values:
+        shapes = [(args.values,)]
+    total = sum(int(torch.Size(s).numel()) for s in shapes)
+    params, grads = make_workload(dev, shapes)
+    opt = RefZE(params, lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1,
+                optimized=not eager)
+    for p_, g_ in zip(params, grads):
+        p_.grad = g_
+    t0 = time.perf_counter()
+    for _ in range(args.warmup):
+        opt.step()
+    torch.cuda.synchronize()
+    warm_s = time.perf_counter() - t0
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        opt.step()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / args.steps
+    print(json.dumps({"metric": METRIC, "value": total / (ms / 1e3), "unit": UNIT, "n_gpus": 1,
+                      "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+                      "higher_is_better": True, "impl": impl, "dtype": "f32",
+                      "data": "synthetic",
+                      "config": {"workload": WORKLOAD, "values": total, "tensors": len(shapes)},
+                      "warmup_seconds": warm_s}), flush=True)
+
+
 def run_ours(args, rank, world, local):
     from adamw4bit_b200 import ZEEDENAdamW4Bit, _native
     from adamw4bit_b200.zero import ZeRO1AdamW4Bit
@@ -377,7 +428,8 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "reference-gpu", "reference-gpu-eager"],
+                    default="ours")
     ap.add_argument("--rounds", type=int, default=4, help="ZeRO-1 gather rounds")
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--cpu-sample", type=int, default=1 << 27,
@@ -390,6 +442,10 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
+    if args.impl in ("reference-gpu", "reference-gpu-eager"):
+        run_reference_gpu(args, int(os.environ.get("RANK", "0")),
+                          eager=args.impl == "reference-gpu-eager")
+        return
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
         run_reference(args, rank, int(os.environ.get("WORLD_SIZE", "1")))
