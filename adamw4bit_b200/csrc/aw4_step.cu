@@ -31,7 +31,7 @@
 namespace aw4 {
 
 constexpr int kMaxTensors = 300;   // tensors per launch (kernel parameter space)
-constexpr int kMaxHypers = 8;      // distinct per-step scalar sets per launch
+constexpr int kMaxHypers = 8;      // distinct per-step scalar sets per FP32-state launch
 constexpr int kSubBlocks = 2;      // blocks each 16-lane group takes per tile
 constexpr int kStepBlocksPerTile = kBlocksPerTile * kSubBlocks;   // 32 blocks = 4096 values
 
@@ -48,7 +48,7 @@ struct KDesc {
     int32_t nblocks;
     int32_t tile_begin;
     uint32_t ordinal;
-    int32_t hyper;
+    int32_t pad;
 };
 
 // One hyper-parameter set as the kernel reads it: the caller's aw4_hyper plus
@@ -63,9 +63,12 @@ struct HyperDev {
     uint64_t m1_key, m2_key;
 };
 
+// One launch covers tensors of one hyper-parameter set, so every scalar is
+// read from the parameter bank at a fixed offset (an instruction operand, no
+// load); the host issues one launch per distinct set.
 struct StepLaunch {
     aw4_scheme m1, m2;
-    HyperDev hyper[kMaxHypers];
+    HyperDev h;
     int32_t n_tensors, n_tiles, eden;
     float one;                        // 1.0, read at run time (packed additions)
     KDesc t[kMaxTensors];
@@ -178,7 +181,7 @@ step_kernel(const __grid_constant__ StepLaunch L) {
     for (int tile = blockIdx.x; tile < L.n_tiles; tile += gridDim.x) {
         while (ti + 1 < L.n_tensors && L.t[ti + 1].tile_begin <= tile) ++ti;
         const KDesc& D = L.t[ti];
-        const HyperDev& H = L.hyper[D.hyper];
+        const HyperDev& H = L.h;
         const int blk0 = (tile - D.tile_begin) * kStepBlocksPerTile + group;
 #pragma unroll 1
         for (int sb = 0; sb < kSubBlocks; ++sb) {
@@ -490,63 +493,65 @@ extern "C" int32_t aw4_step_quantized(const aw4_scheme* m1, const aw4_scheme* m2
     int grid_cap = grid_for(fn, device, 1 << 30);
     if (max_ctas > 0) grid_cap = std::min(grid_cap, max_ctas);
 
-    // Pack tensors into launches of <= kMaxTensors tensors / kMaxHypers scalar sets.
+    // Distinct hyper-parameter sets (equal contents count as one), then one
+    // or more launches of <= kMaxTensors tensors per set.
+    std::vector<int> set_of(n_tensors, -1), reps;
+    for (int i = 0; i < n_tensors; ++i) {
+        for (size_t k = 0; k < reps.size(); ++k)
+            if (tensors[reps[k]].hyper == tensors[i].hyper ||
+                std::memcmp(&hypers[tensors[reps[k]].hyper], &hypers[tensors[i].hyper],
+                            sizeof(aw4_hyper)) == 0) {
+                set_of[i] = (int)k;
+                break;
+            }
+        if (set_of[i] < 0) {
+            set_of[i] = (int)reps.size();
+            reps.push_back(i);
+        }
+    }
     StepLaunch* L = new StepLaunch;
     std::memset(L, 0, sizeof(StepLaunch));
     L->m1 = *m1;
     L->m2 = *m2;
     L->eden = eden ? 1 : 0;
     L->one = 1.0f;
-    int i = 0;
     int32_t rc = AW4_OK;
-    while (i < n_tensors && rc == AW4_OK) {
-        L->n_tensors = 0;
-        L->n_tiles = 0;
-        int nh = 0;
-        std::vector<int> hsrc;
-        for (; i < n_tensors && L->n_tensors < kMaxTensors; ++i) {
-            const aw4_qtensor& t = tensors[i];
-            if (t.numel == 0) continue;
-            int h = -1;
-            for (int k = 0; k < nh; ++k)
-                if (hsrc[k] == t.hyper ||
-                    std::memcmp(&hypers[hsrc[k]], &hypers[t.hyper], sizeof(aw4_hyper)) == 0) {
-                    h = k;
+    for (size_t set = 0; set < reps.size() && rc == AW4_OK; ++set) {
+        L->h = hyper_dev(hypers[tensors[reps[set]].hyper], *m2);
+        int i = 0;
+        while (i < n_tensors && rc == AW4_OK) {
+            L->n_tensors = 0;
+            L->n_tiles = 0;
+            for (; i < n_tensors && L->n_tensors < kMaxTensors; ++i) {
+                const aw4_qtensor& t = tensors[i];
+                if (t.numel == 0 || set_of[i] != (int)set) continue;
+                KDesc& d = L->t[L->n_tensors++];
+                d.param = t.param;
+                d.grad = t.grad;
+                d.c1 = t.m1_codes;
+                d.s1 = t.m1_scales;
+                d.c2 = t.m2_codes;
+                d.s2 = t.m2_scales;
+                d.d1 = t.m1_draws;
+                d.d2 = t.m2_draws;
+                d.elem_offset = t.elem_offset;
+                d.nblocks = (int32_t)(t.numel / AW4_BLOCK);
+                d.tile_begin = L->n_tiles;
+                d.ordinal = t.ordinal;
+                const int64_t tiles = (d.nblocks + kStepBlocksPerTile - 1) / kStepBlocksPerTile;
+                if ((int64_t)L->n_tiles + tiles > 0x7fffffffLL) {
+                    rc = fail(AW4_ERR_INVALID, "launch exceeds 2^31 tiles");
                     break;
                 }
-            if (h < 0) {
-                if (nh == kMaxHypers) break;
-                h = nh++;
-                hsrc.push_back(t.hyper);
-                L->hyper[h] = hyper_dev(hypers[t.hyper], *m2);
+                L->n_tiles += (int32_t)tiles;
             }
-            KDesc& d = L->t[L->n_tensors++];
-            d.param = t.param;
-            d.grad = t.grad;
-            d.c1 = t.m1_codes;
-            d.s1 = t.m1_scales;
-            d.c2 = t.m2_codes;
-            d.s2 = t.m2_scales;
-            d.d1 = t.m1_draws;
-            d.d2 = t.m2_draws;
-            d.elem_offset = t.elem_offset;
-            d.nblocks = (int32_t)(t.numel / AW4_BLOCK);
-            d.tile_begin = L->n_tiles;
-            d.ordinal = t.ordinal;
-            d.hyper = h;
-            const int64_t tiles = (d.nblocks + kStepBlocksPerTile - 1) / kStepBlocksPerTile;
-            if ((int64_t)L->n_tiles + tiles > 0x7fffffffLL) {
-                rc = fail(AW4_ERR_INVALID, "launch exceeds 2^31 tiles");
-                break;
-            }
-            L->n_tiles += (int32_t)tiles;
+            if (rc != AW4_OK || L->n_tensors == 0) break;
+            const int grid = std::min(grid_cap, L->n_tiles);
+            fn<<<grid, kThreads, 0, s>>>(*L);
+            note_launch();
+            cudaError_t e = cudaGetLastError();
+            if (e != cudaSuccess) rc = fail(AW4_ERR_CUDA, "step launch: %s", cudaGetErrorString(e));
         }
-        if (rc != AW4_OK || L->n_tensors == 0) break;
-        const int grid = std::min(grid_cap, L->n_tiles);
-        fn<<<grid, kThreads, 0, s>>>(*L);
-        note_launch();
-        cudaError_t e = cudaGetLastError();
-        if (e != cudaSuccess) rc = fail(AW4_ERR_CUDA, "step launch: %s", cudaGetErrorString(e));
     }
     delete L;
     return rc;
