@@ -44,6 +44,7 @@ struct KDesc {
     float* s2;
     const float* d1;
     const float* d2;
+    void* pc;            // BF16 model copy of the updated params, or null
     int64_t elem_offset;
     int32_t nblocks;
     int32_t tile_begin;
@@ -235,6 +236,7 @@ step_kernel(const __grid_constant__ StepLaunch L) {
                 for (int i = 0; i < 8; ++i) p[i] = Elem<PT>::round(p[i]);
                 vadd8(p, q, p, one);                 // p.addcdiv_(m1, den, -lr/bc1)
                 Elem<PT>::store8(D.param, e0, p);
+                if (D.pc != nullptr) Elem<AW4_BF16>::store8(D.pc, e0, p);   // model copy
                 if (M1 != AW4_RTN) load_uniforms(u, D.d1, H.m1_key, H, D, e0, true);
                 float ns1, ns2;
                 const uint32_t c1 =
@@ -261,7 +263,10 @@ step_kernel(const __grid_constant__ StepLaunch L) {
 #pragma unroll
             for (int i = 0; i < 8; ++i) p[i] = Elem<PT>::round(p[i]);
             vadd8(p, q, p, one);                     // p.addcdiv_(m1, den, -lr/bc1)
-            if (active) Elem<PT>::store8(D.param, e0, p);
+            if (active) {
+                Elem<PT>::store8(D.param, e0, p);
+                if (D.pc != nullptr) Elem<AW4_BF16>::store8(D.pc, e0, p);   // model copy
+            }
 
             // re-encode m1 (adamw.py:764-771)
             if (M1 != AW4_RTN) load_uniforms(u, D.d1, H.m1_key, H, D, e0, active);
@@ -485,6 +490,9 @@ extern "C" int32_t aw4_step_quantized(const aw4_scheme* m1, const aw4_scheme* m2
             return fail(AW4_ERR_INVALID, "tensor %d: elem_offset must be a multiple of 128", i);
         if (t.hyper < 0 || t.hyper >= n_hypers)
             return fail(AW4_ERR_INVALID, "tensor %d: hyper index %d out of range", i, t.hyper);
+        if (t.param_copy && (param_dtype != AW4_F32 || !aligned(t.param_copy, 16)))
+            return fail(AW4_ERR_INVALID,
+                        "tensor %d: a BF16 param copy needs FP32 params and 16-byte alignment", i);
         (void)pb; (void)gb;
     }
     DeviceGuard guard(device);
@@ -534,6 +542,7 @@ extern "C" int32_t aw4_step_quantized(const aw4_scheme* m1, const aw4_scheme* m2
                 d.s2 = t.m2_scales;
                 d.d1 = t.m1_draws;
                 d.d2 = t.m2_draws;
+                d.pc = t.param_copy;
                 d.elem_offset = t.elem_offset;
                 d.nblocks = (int32_t)(t.numel / AW4_BLOCK);
                 d.tile_begin = L->n_tiles;

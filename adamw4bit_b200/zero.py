@@ -12,6 +12,11 @@ elements it owns.  A step is:
      the number of ranks);
   2. NCCL all-gathers the updated parameters over NVLink, in place.
 
+With ``master_weights=True`` the parameters are a BF16 model and each rank
+keeps FP32 master weights for the elements it owns only: the fused kernel
+updates the masters and writes bf16(master) into the model in the same pass,
+and the all-gather moves the BF16 model (2 bytes per value instead of 4).
+
 Ownership is block-cyclic over ``rounds`` rounds: round i covers the flat
 range [i*W*c, (i+1)*W*c) and rank r owns its r-th c-element slice, so each
 round's all-gather writes one contiguous range and can run while the kernel
@@ -95,12 +100,14 @@ class ZeRO1AdamW4Bit:
         rounds: number of pipelined gather rounds.
         quant_rng_seed: Philox seed for SR recipes.
         reserve_sms: SMs the update grid leaves to the concurrent all-gather.
+        master_weights: the parameters are a BF16 model; keep FP32 master
+            weights for the owned elements and gather the BF16 model.
     """
 
     def __init__(self, params, *, recipe: str = "ze-eden", lr: float = 1e-3,
                  betas=(0.9, 0.95), eps: float = 1e-8, weight_decay: float = 0.1,
                  process_group=None, rounds: int = 4, quant_rng_seed: int = 0,
-                 reserve_sms: int = 16):
+                 reserve_sms: int = 16, master_weights: bool = False):
         self.params = [p for p in params]
         if not self.params:
             raise ValueError("ZeRO1AdamW4Bit needs parameters")
@@ -118,6 +125,9 @@ class ZeRO1AdamW4Bit:
             if p.numel() % 128 or p.numel() < 4096:
                 raise NotImplementedError("ZeRO1AdamW4Bit shards quantized tensors only "
                                           "(numel >= 4096, multiple of 128)")
+        if master_weights and dtype != torch.bfloat16:
+            raise ValueError("master_weights=True needs BF16 parameters (the model copy)")
+        self.master_weights = master_weights
         self.device, self.dtype = dev, dtype
         self.keys = ((quant_rng_seed + _M1_OFFSET) % _MAX_SEED,
                      (quant_rng_seed + _M2_OFFSET) % _MAX_SEED)
@@ -135,6 +145,14 @@ class ZeRO1AdamW4Bit:
         self.owned = plan.owned
         # state for the owned elements, one flat buffer per kind
         n_own = plan.state_numel()
+        self.master = None
+        if master_weights:
+            # FP32 masters of the owned elements, laid out like the state buffers
+            self.master = torch.zeros(n_own, dtype=torch.float32, device=dev)
+            for segs in plan.segments:
+                for ti, s, n, so in segs:
+                    src = self.params[ti].detach().reshape(-1)[s:s + n]
+                    self.master[so:so + n].copy_(src.float())
         self.m1_codes = torch.empty(n_own // 2, dtype=torch.uint8, device=dev)
         self.m2_codes = torch.empty(n_own // 2, dtype=torch.uint8, device=dev)
         self.m1_scales = torch.empty(n_own // 128, dtype=torch.float32, device=dev)
@@ -165,7 +183,7 @@ class ZeRO1AdamW4Bit:
                                      self.keys[1]))
         dev = self.device
         cur = torch.cuda.current_stream(dev)
-        pdt = N.DTYPE_CODES[self.dtype]
+        pdt = N.DTYPE_CODES[torch.float32 if self.master_weights else self.dtype]
         esz_p = self.flat.element_size()
         grads = [p.grad for p in self.params]
         if any(g is None for g in grads):
@@ -176,11 +194,16 @@ class ZeRO1AdamW4Bit:
             descs = []
             for ti, s, n, so in segs:
                 p, g = self.params[ti], grads[ti]
+                model = p.data_ptr() + s * esz_p
+                if self.master_weights:   # update the FP32 master, write the BF16 model
+                    target, copy = self.master.data_ptr() + so * 4, model
+                else:
+                    target, copy = model, None
                 descs.append(N.QTensor(
-                    p.data_ptr() + s * esz_p, g.data_ptr() + s * g.element_size(),
+                    target, g.data_ptr() + s * g.element_size(),
                     self.m1_codes.data_ptr() + so // 2, self.m1_scales.data_ptr() + (so // 128) * 4,
                     self.m2_codes.data_ptr() + so // 2, self.m2_scales.data_ptr() + (so // 128) * 4,
-                    None, None, n, s, ti, 0))
+                    None, None, n, s, ti, 0, copy))
             if descs:
                 arr = (N.QTensor * len(descs))(*descs)
                 if self.launch_timings is not None:

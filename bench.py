@@ -7,8 +7,10 @@ Workload: the Llama-3-8B parameter set (vocab 128256, d 4096, 32 layers, ffn
 14336, 32/8 heads, untied head: 291 tensors, 8.03 B values, all quantized),
 FP32 master parameters, BF16 gradients N(0, 1e-4), ZEEDENAdamW4Bit (NF4 m1 +
 zero-exclusive Dyn4 m2 with EDEN).  N=1 steps the whole set through the public
-optimizer API; N>1 shards it ZeRO-1 style (ZeRO1AdamW4Bit) and all-gathers the
-updated FP32 parameters with NCCL.  Synthetic data, random-init weights.
+optimizer API; N>1 shards it ZeRO-1 style (ZeRO1AdamW4Bit): FP32 master
+weights sharded over the ranks, a BF16 model copy written by the update kernel
+and all-gathered with NCCL (``--gather fp32`` gathers FP32 parameters instead).
+Synthetic data, random-init weights.
 
 A step is one pass of the optimizer over every parameter.  ``value`` is the
 whole-job elements/s with everything resident in HBM (the 56 GB working set
@@ -145,11 +147,11 @@ def barrier(world: int):
     torch.cuda.synchronize()
 
 
-def make_workload(dev, shapes, seed=0):
+def make_workload(dev, shapes, seed=0, param_dtype=torch.float32):
     g = torch.Generator(device=dev).manual_seed(seed)
     params, grads = [], []
     for s in shapes:
-        p = torch.nn.Parameter(torch.randn(s, device=dev, generator=g) * 0.02)
+        p = torch.nn.Parameter((torch.randn(s, device=dev, generator=g) * 0.02).to(param_dtype))
         gr = (torch.randn(s, device=dev, generator=g) * 1e-4).to(torch.bfloat16)
         p.grad_dtype = None  # FP32 parameter, BF16 gradient
         params.append(p)
@@ -269,15 +271,21 @@ def run_ours(args, rank, world, local):
     if args.values:
         shapes = [(args.values,)]   # single-tensor case (profiling)
     total = sum(int(torch.Size(s).numel()) for s in shapes)
-    params, grads = make_workload(dev, shapes)
+    master = world > 1 and args.gather == "bf16"
+    params, grads = make_workload(dev, shapes,
+                                  param_dtype=torch.bfloat16 if master else torch.float32)
     if world == 1:
         opt = ZEEDENAdamW4Bit(params, lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
         step_fn = opt.step
         updated_per_rank = total
     else:
-        opt = ZeRO1AdamW4Bit(params, recipe="ze-eden", rounds=args.rounds)
+        # FP32 masters sharded over the ranks; with --gather bf16 the model is
+        # BF16 (written by the update kernel) and the all-gather moves 2 B/value
+        opt = ZeRO1AdamW4Bit(params, recipe="ze-eden", rounds=args.rounds,
+                             master_weights=master, reserve_sms=args.reserve_sms)
         step_fn = opt.step
         updated_per_rank = opt.owned_numel()
+    b_per_elem = B_PER_ELEM + (2 if master else 0)   # + the BF16 model copy write
     for p, g in zip(params, grads):
         p.grad = g
     for _ in range(args.warmup):
@@ -317,15 +325,15 @@ def run_ours(args, rank, world, local):
         hbm_peak, peak_src = 6650.0, "fallback"
     per_launch_ms = kernel_ms / max(1, len(timings))
     per_launch_elems = kernel_elems / max(1, len(timings))
-    achieved = per_launch_elems * B_PER_ELEM / (per_launch_ms / 1e3) / 1e9
+    achieved = per_launch_elems * b_per_elem / (per_launch_ms / 1e3) / 1e9
     tr = traffic_record()
     traffic = None
-    if tr and tr.get("bytes_per_value"):
+    if tr and tr.get("bytes_per_value") and not master:   # captured on the N=1 workload
         traffic = tr["bytes_per_value"] * per_launch_elems
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                 "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
                 "peak_source": peak_src,
-                "algorithmic_bytes_per_value": B_PER_ELEM,
+                "algorithmic_bytes_per_value": b_per_elem,
                 "kernel": "aw4::step_kernel<F32,BF16,RTN,RTN> (fused decode+AdamW+encode)",
                 "launch_ms": round(per_launch_ms, 4), "values_per_launch": int(per_launch_elems)}
 
@@ -340,8 +348,10 @@ def run_ours(args, rank, world, local):
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                 "dtype": "f32", "data": "synthetic",
                 "config": {"workload": WORKLOAD, "values": total, "tensors": len(shapes),
-                           "param_dtype": "fp32", "grad_dtype": "bf16", "recipe": "ZE-EDEN",
-                           "parallelism": "single GPU" if world == 1 else f"zero1-dp{world}",
+                           "param_dtype": "fp32 master + bf16 model copy" if master else "fp32",
+                           "grad_dtype": "bf16", "recipe": "ZE-EDEN",
+                           "parallelism": "single GPU" if world == 1 else
+                           f"zero1-dp{world}, {'bf16 model' if master else 'fp32'} all-gather",
                            "l2": "no flush: 56 GB working set >> 126 MB L2"},
                 "roofline": roofline,
                 "update_only": {"values_per_rank": updated_per_rank,
@@ -431,6 +441,11 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference", "reference-gpu", "reference-gpu-eager"],
                     default="ours")
     ap.add_argument("--rounds", type=int, default=4, help="ZeRO-1 gather rounds")
+    ap.add_argument("--reserve-sms", type=int, default=16,
+                    help="N>1: SMs the update grid leaves to the concurrent all-gather")
+    ap.add_argument("--gather", choices=["bf16", "fp32"], default="bf16",
+                    help="N>1: all-gather a BF16 model copy of the FP32 masters (default) or "
+                         "the FP32 parameters themselves")
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--cpu-sample", type=int, default=1 << 27,
                     help="values in the CPU-oracle sample (0: skip)")

@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define AW4_ABI_VERSION 1
+#define AW4_ABI_VERSION 2
 #define AW4_BLOCK 128          /* elements per quantization block (4-bit default) */
 #define AW4_LUT_BINS 1024      /* maximum uniform bins over [-1, 1] for the rounding search */
 
@@ -103,6 +103,9 @@ typedef struct aw4_qtensor {
     int64_t elem_offset;           /* index of element 0 in the whole tensor (Philox) */
     uint32_t ordinal;              /* parameter ordinal (Philox counter word) */
     int32_t hyper;                 /* index into the aw4_hyper array */
+    void* param_copy;              /* NULL, or numel BF16 values that receive bf16(updated
+                                    * param): the model copy of FP32 master parameters
+                                    * (16-byte aligned; FP32 params only) */
 } aw4_qtensor;
 
 /* One tensor with FP32 moments (numel arbitrary). */

@@ -24,7 +24,7 @@ def _make(dev, seed=0):
     return params, grads
 
 
-def _worker(rank, world, port, recipe, rounds, q):
+def _worker(rank, world, port, recipe, rounds, q, master=False):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     import datetime
 
@@ -38,10 +38,14 @@ def _worker(rank, world, port, recipe, rounds, q):
         dist.init_process_group("nccl", rank=rank, world_size=world,
                                 timeout=datetime.timedelta(seconds=120), device_id=dev)
         vals, grads = _make(dev)
-        params = [torch.nn.Parameter(v.clone()) for v in vals]
+        if master:   # a BF16 model; FP32 masters start from its values
+            vals = [v.to(torch.bfloat16).float() for v in vals]
+        model_dtype = torch.bfloat16 if master else torch.float32
+        params = [torch.nn.Parameter(v.clone().to(model_dtype)) for v in vals]
         for p in params:
             p.grad_dtype = None
-        opt = ZeRO1AdamW4Bit(params, recipe=recipe, rounds=rounds, quant_rng_seed=9)
+        opt = ZeRO1AdamW4Bit(params, recipe=recipe, rounds=rounds, quant_rng_seed=9,
+                             master_weights=master)
         for step_grads in grads:
             for p, g in zip(params, step_grads):
                 p.grad = g
@@ -59,8 +63,20 @@ def _worker(rank, world, port, recipe, rounds, q):
                 p.grad = g
             single.step()
         torch.cuda.synchronize()
-        ok = all(torch.equal(a.detach().view(torch.int32), b.detach().view(torch.int32))
-                 for a, b in zip(params, ref))
+        if master:
+            # the gathered BF16 model is bf16(the unsharded FP32 params) everywhere,
+            # and this rank's FP32 masters equal the unsharded params it owns
+            ok = all(torch.equal(a.detach().view(torch.int16),
+                                 b.detach().to(torch.bfloat16).view(torch.int16))
+                     for a, b in zip(params, ref))
+            for segs in opt.plan.segments:
+                for ti, s0, n, so in segs:
+                    want = ref[ti].detach().reshape(-1)[s0:s0 + n]
+                    ok = ok and torch.equal(opt.master[so:so + n].view(torch.int32),
+                                            want.view(torch.int32))
+        else:
+            ok = all(torch.equal(a.detach().view(torch.int32), b.detach().view(torch.int32))
+                     for a, b in zip(params, ref))
         q.put((rank, ok, None))
     except Exception as e:  # report to the parent instead of hanging it
         q.put((rank, False, repr(e)))
@@ -69,17 +85,48 @@ def _worker(rank, world, port, recipe, rounds, q):
             dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("recipe,rounds", [("ze-eden", 1), ("ze-eden", 3), ("zip-sr", 2)])
-def test_zero1_two_gpus_matches_single_gpu_bit_exact(recipe, rounds):
+@pytest.mark.parametrize("recipe,rounds,master", [("ze-eden", 1, False), ("ze-eden", 3, False),
+                                                  ("zip-sr", 2, False), ("ze-eden", 2, True)])
+def test_zero1_two_gpus_matches_single_gpu_bit_exact(recipe, rounds, master):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29600 + (os.getpid() % 500)
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, recipe, rounds, q)) for r in range(2)]
+    port = 29600 + (os.getpid() % 500) + (7 if master else 0)
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, recipe, rounds, q, master))
+             for r in range(2)]
     for p in procs:
         p.start()
     results = [q.get(timeout=300) for _ in procs]
     for p in procs:
         p.join(timeout=60)
     assert all(ok for _, ok, _ in results), results
+
+
+def test_zero1_master_weights_on_one_gpu_matches_fp32_step():
+    """master_weights without a process group (one rank): FP32 masters equal
+    the FP32 optimizer's params and the BF16 model equals their bf16 cast."""
+    from adamw4bit_b200 import ZEEDENAdamW4Bit
+    from adamw4bit_b200.zero import ZeRO1AdamW4Bit
+    dev = torch.device("cuda", 0)
+    vals, grads = _make(dev, seed=3)
+    vals = [v.to(torch.bfloat16).float() for v in vals]
+    model = [torch.nn.Parameter(v.to(torch.bfloat16)) for v in vals]
+    fp32 = [torch.nn.Parameter(v.clone()) for v in vals]
+    for p in fp32:
+        p.grad_dtype = None
+    opt = ZeRO1AdamW4Bit(model, recipe="ze-eden", rounds=2, master_weights=True)
+    ref = ZEEDENAdamW4Bit(fp32)
+    for step_grads in grads:
+        for a, b, g in zip(model, fp32, step_grads):
+            a.grad = g
+            b.grad = g
+        opt.step()
+        ref.step()
+    torch.cuda.synchronize()
+    for a, b in zip(model, fp32):
+        assert torch.equal(a.detach().view(torch.int16), b.detach().to(torch.bfloat16).view(torch.int16))
+    for segs in opt.plan.segments:
+        for ti, s0, n, so in segs:
+            want = fp32[ti].detach().reshape(-1)[s0:s0 + n]
+            assert torch.equal(opt.master[so:so + n].view(torch.int32), want.view(torch.int32))
