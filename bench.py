@@ -239,8 +239,13 @@ def run_reference_gpu(args, rank, eager: bool):
     for p_, g_ in zip(params, grads):
         p_.grad = g_
     t0 = time.perf_counter()
-    for _ in range(args.warmup):
-        opt.step()
+    try:
+        for _ in range(args.warmup):
+            opt.step()
+    except TypeError as exc:   # the reference needs torch >= 2.13 for its compiled path
+        print(json.dumps({"impl": impl, "unavailable": f"reference step failed on torch "
+                                                        f"{torch.__version__}: {exc}"}))
+        return
     torch.cuda.synchronize()
     warm_s = time.perf_counter() - t0
     e0 = torch.cuda.Event(enable_timing=True)
