@@ -19,8 +19,10 @@ same metric through the public API with the gradients copied in from pinned
 host memory and the updated parameters copied back each step.
 ``--impl reference`` times the CPU oracle port of the reference algorithm on
 the host's cores on a bounded sample of the same workload.  ``--impl
-reference-gpu`` (and ``reference-gpu-eager``) time the reference's own CUDA
-path from the offline install under baseline/_ref, for comparison only.
+reference-gpu`` / ``reference-gpu-eager`` / ``reference-cpu`` /
+``reference-cpu-eager`` time the reference's own implementation (from the
+offline install under baseline/_ref) on the GPU or on the host cores, for
+comparison only.
 """
 
 from __future__ import annotations
@@ -210,26 +212,33 @@ def run_reference(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
-def run_reference_gpu(args, rank, eager: bool):
-    """The reference's own CUDA path on this GPU (the "GPU bar"): its
-    ZEEDENAdamW4Bit with optimized=True (torch.compile per 512 Ki chunk) or,
-    with ``eager``, its eager path, on the same workload.  Imported from the
-    offline install under baseline/_ref; not part of the product."""
+def run_reference_torch(args, rank, device: str, eager: bool):
+    """The reference's own implementation (its ZEEDENAdamW4Bit), for
+    comparison only: on CUDA (the "GPU bar") with optimized=True
+    (torch.compile per 512 Ki chunk) or its eager path; on the host CPU with
+    all threads, eager or chunked (optimized=True).  Imported from the offline
+    install under baseline/_ref; not part of the product.  The CPU runs
+    default to config 1's tensor (4096 x 4096)."""
     if rank != 0:
         return
     ref = os.path.join(ROOT, "baseline", "_ref")
-    impl = "reference-gpu-eager" if eager else "reference-gpu"
+    impl = f"reference-{'gpu' if device == 'cuda' else 'cpu'}{'-eager' if eager else ''}"
     if not os.path.isdir(os.path.join(ref, "adamw4bit")):
         print(json.dumps({"impl": impl, "unavailable": "baseline/_ref is not installed"}))
         return
     sys.path.insert(0, ref)
     from adamw4bit import ZEEDENAdamW4Bit as RefZE
 
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    shapes = llama3_8b_shapes()
-    if args.layers is not None:
-        shapes = shapes[:1 + 9 * args.layers] + shapes[-2:]
+    if device == "cuda":
+        dev = torch.device("cuda", 0)
+        torch.cuda.set_device(dev)
+        shapes = llama3_8b_shapes()
+        if args.layers is not None:
+            shapes = shapes[:1 + 9 * args.layers] + shapes[-2:]
+    else:
+        dev = torch.device("cpu")
+        torch.set_num_threads(os.cpu_count() or 1)
+        shapes = [(4096, 4096)]
     if args.values:
         shapes = [(args.values,)]
     total = sum(int(torch.Size(s).numel()) for s in shapes)
@@ -246,22 +255,35 @@ def run_reference_gpu(args, rank, eager: bool):
         print(json.dumps({"impl": impl, "unavailable": f"reference step failed on torch "
                                                         f"{torch.__version__}: {exc}"}))
         return
-    torch.cuda.synchronize()
-    warm_s = time.perf_counter() - t0
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(args.steps):
-        opt.step()
-    e1.record()
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / args.steps
+    if device == "cuda":
+        torch.cuda.synchronize()
+        warm_s = time.perf_counter() - t0
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            opt.step()
+        e1.record()
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        extra = {}
+    else:
+        warm_s = time.perf_counter() - t0
+        times = []
+        for _ in range(args.steps):
+            t1 = time.perf_counter()
+            opt.step()
+            times.append(time.perf_counter() - t1)
+        ms = statistics.median(times) * 1e3
+        extra = {"cores": torch.get_num_threads(), "timing": "median wall time per step"}
     print(json.dumps({"metric": METRIC, "value": total / (ms / 1e3), "unit": UNIT, "n_gpus": 1,
                       "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
                       "higher_is_better": True, "impl": impl, "dtype": "f32",
                       "data": "synthetic",
-                      "config": {"workload": WORKLOAD, "values": total, "tensors": len(shapes)},
-                      "warmup_seconds": warm_s}), flush=True)
+                      "config": {"workload": WORKLOAD if device == "cuda" else
+                                 "4096x4096 FP32 param, BF16 grads, ZE-EDEN",
+                                 "values": total, "tensors": len(shapes)},
+                      "warmup_seconds": warm_s, **extra}), flush=True)
 
 
 def run_ours(args, rank, world, local):
@@ -443,7 +465,8 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--impl", choices=["ours", "reference", "reference-gpu", "reference-gpu-eager"],
+    ap.add_argument("--impl", choices=["ours", "reference", "reference-gpu", "reference-gpu-eager",
+                                       "reference-cpu", "reference-cpu-eager"],
                     default="ours")
     ap.add_argument("--rounds", type=int, default=4, help="ZeRO-1 gather rounds")
     ap.add_argument("--reserve-sms", type=int, default=16,
@@ -462,9 +485,10 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("warning: fewer than 3 warm-up steps", file=sys.stderr)
-    if args.impl in ("reference-gpu", "reference-gpu-eager"):
-        run_reference_gpu(args, int(os.environ.get("RANK", "0")),
-                          eager=args.impl == "reference-gpu-eager")
+    if args.impl.startswith("reference-"):
+        run_reference_torch(args, int(os.environ.get("RANK", "0")),
+                            "cuda" if "gpu" in args.impl else "cpu",
+                            eager=args.impl.endswith("-eager"))
         return
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))
