@@ -1,11 +1,12 @@
 // aw4_step.cu -- the fused 4-bit AdamW step (one launch over many tensors).
 //
-// Work unit: a tile of 16 quantization blocks (2048 values) of one tensor.
+// Work unit: a tile of 64 quantization blocks (8192 values) of one tensor.
 // A persistent grid of 256-thread CTAs walks the tiles of every tensor in the
-// launch; each 16-lane group owns one 128-value block and each lane 8
-// consecutive values, so a block is decoded, updated and re-encoded entirely
-// in registers (block absmax by shuffles, EDEN sums through shared memory)
-// with exactly one read and one write of every byte of state:
+// launch; each warp takes a strip of 8 blocks, two at a time: each 16-lane
+// group owns one 128-value block and each lane 8 consecutive values, so a
+// block is decoded, updated and re-encoded entirely in registers (block
+// absmax by a warp reduction, EDEN sums through shared memory) with exactly
+// one read and one write of every byte of state:
 //   read  param, grad, m1/m2 packed codes, m1/m2 block scales
 //   write param,       m1/m2 packed codes, m1/m2 block scales
 //
@@ -32,8 +33,15 @@ namespace aw4 {
 
 constexpr int kMaxTensors = 300;   // tensors per launch (kernel parameter space)
 constexpr int kMaxHypers = 8;      // distinct per-step scalar sets per FP32-state launch
-constexpr int kSubBlocks = 2;      // blocks each 16-lane group takes per tile
-constexpr int kStepBlocksPerTile = kBlocksPerTile * kSubBlocks;   // 32 blocks = 4096 values
+// A tile is 64 blocks (8192 values) of one tensor, taken as 4 sub-blocks of
+// 16 consecutive blocks; in each, warp w takes blocks 2w and 2w+1 (one per
+// 16-lane group).  The tile's 64 new scales per moment are collected in
+// shared memory and written by two warps as 256 contiguous bytes each:
+// measured on this kernel's load/store skeleton, 4-byte scale stores
+// scattered over warps held the whole stream to 75 % of the copy bandwidth,
+// 32-byte per-warp stores to 85 %, and these 256-byte stores to 99 %.
+constexpr int kSubBlocks = 4;
+constexpr int kStepBlocksPerTile = kSubBlocks * kBlocksPerTile;   // 64 blocks
 
 struct KDesc {
     void* param;
@@ -79,6 +87,7 @@ static_assert(sizeof(StepLaunch) <= 32000, "kernel parameter space");
 struct StepSmem {
     SmemScheme s1, s2;
     float scratch[kThreads / 32][kWarpScratch];
+    float scales[2][kStepBlocksPerTile];   // the tile's new m1 / m2 scales
 };
 // 8-byte table entries (s2), and float4 columns in each warp's EDEN scratch
 static_assert(offsetof(StepSmem, s2) % 16 == 0, "");
@@ -174,7 +183,8 @@ step_kernel(const __grid_constant__ StepLaunch L) {
     const float one = L.one;
     const GroupCtx g = group_ctx(sm.scratch[tid >> 5], lane, one);
     const SchemeRegs r1 = scheme_regs(sm.s1, lane), r2 = scheme_regs(sm.s2, lane);
-    const int group = tid >> 4;
+    const int warp = tid >> 5;
+    const int h = lane >> 4;   // group within the warp
     const int zf2 = L.m2.zero_floor;
 
     // tiles only grow along this loop, so the owning tensor moves forward
@@ -183,10 +193,11 @@ step_kernel(const __grid_constant__ StepLaunch L) {
         while (ti + 1 < L.n_tensors && L.t[ti + 1].tile_begin <= tile) ++ti;
         const KDesc& D = L.t[ti];
         const HyperDev& H = L.h;
-        const int blk0 = (tile - D.tile_begin) * kStepBlocksPerTile + group;
+        const int tile0 = (tile - D.tile_begin) * kStepBlocksPerTile;
 #pragma unroll 1
         for (int sb = 0; sb < kSubBlocks; ++sb) {
-            const int blk = blk0 + sb * kBlocksPerTile;
+            const int slot = kBlocksPerTile * sb + 2 * warp + h;   // block within the tile
+            const int blk = tile0 + slot;
             const bool active = blk < D.nblocks;
             const int64_t e0 = (int64_t)blk * kBlock + 8 * g.j;
 
@@ -247,8 +258,8 @@ step_kernel(const __grid_constant__ StepLaunch L) {
                 __stcs(reinterpret_cast<unsigned int*>(D.c1 + (e0 >> 1)), c1);
                 __stcs(reinterpret_cast<unsigned int*>(D.c2 + (e0 >> 1)), c2);
                 if (g.j == 0) {
-                    __stcs(D.s1 + blk, ns1);
-                    __stcs(D.s2 + blk, ns2);
+                    sm.scales[0][slot] = ns1;
+                    sm.scales[1][slot] = ns2;
                 }
                 continue;
             }
@@ -284,11 +295,25 @@ step_kernel(const __grid_constant__ StepLaunch L) {
                 __stcs(reinterpret_cast<unsigned int*>(D.c1 + (e0 >> 1)), c1);
                 __stcs(reinterpret_cast<unsigned int*>(D.c2 + (e0 >> 1)), c2);
                 if (g.j == 0) {
-                    __stcs(D.s1 + blk, ns1);
-                    __stcs(D.s2 + blk, ns2);
+                    sm.scales[0][slot] = ns1;
+                    sm.scales[1][slot] = ns2;
                 }
             }
         }
+        // the tile's scales: warp 0 writes m1's, warp 1 m2's, 2 per lane
+        __syncthreads();
+        if (warp < 2) {
+            const int tb = tile0 + 2 * lane;
+            float* dst = (warp == 0 ? D.s1 : D.s2) + tb;
+            const float2 v = reinterpret_cast<const float2*>(sm.scales[warp])[lane];
+            if (tb + 1 < D.nblocks && (reinterpret_cast<uintptr_t>(dst) & 7u) == 0) {
+                __stcs(reinterpret_cast<float2*>(dst), v);
+            } else {
+                if (tb < D.nblocks) __stcs(dst, v.x);
+                if (tb + 1 < D.nblocks) __stcs(dst + 1, v.y);
+            }
+        }
+        __syncthreads();   // the buffer is refilled by the next tile
     }
 }
 
