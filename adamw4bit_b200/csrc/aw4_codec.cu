@@ -53,9 +53,19 @@ quantize_kernel(const __grid_constant__ aw4_scheme scheme, int eden, const float
                 philox_uniform8(key, step, ordinal, (uint64_t)e0, u);
             }
         }
+        // the step kernel's dispatch: one warp vote selects the branch-free
+        // encoder when every lane meets its preconditions (so the exhaustive
+        // codec tests cover both encoders)
         float s;
-        const uint32_t c = encode_block<MODE>(S, R, g, v, lane_absmax(v), u, scheme.zero_floor, eden,
-                                              sr_bias, sr_eps, &s);
+        const float amax = lane_absmax(v);
+        const float sc = max_nan(group_max16(amax), kScaleFloor);
+        bool ok = sc <= kMarksteinMaxDivisor;   // false for NaN / inf
+        if (MODE != AW4_RTN || eden) ok = none_tiny_warp(v, ok);
+        const uint32_t c = __all_sync(0xffffffffu, ok)
+                               ? encode_fast<MODE>(S, R, g, v, sc, u, scheme.zero_floor, eden,
+                                                   sr_bias, sr_eps, &s)
+                               : encode_block<MODE>(S, R, g, v, amax, u, scheme.zero_floor, eden,
+                                                    sr_bias, sr_eps, &s);
         if (active) {
             reinterpret_cast<uint32_t*>(codes)[e0 >> 3] = c;
             if (g.j == 0) scales[blk] = s;

@@ -446,6 +446,28 @@ __device__ __forceinline__ int lut_search(const SmemScheme& s, const SchemeRegs&
     return count - ge;
 }
 
+// lut_search over a lane's 8 values, the bin indices computed pairwise by
+// packed round-toward-zero FMAs.
+__device__ __forceinline__ void lut_search8(const SchemeRegs& r, const float x[8], int code[8]) {
+    const f2 hh = pk2(r.half, r.half), bb = pk2(r.bias, r.bias);
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+        f2 t;
+        asm("fma.rz.f32x2 %0, %1, %2, %3;" : "=l"(t) : "l"(pk2(x[i], x[i + 1])), "l"(hh), "l"(bb));
+        float b0, b1;
+        upk2(t, b0, b1);
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const uint32_t addr = __float_as_uint(k ? b1 : b0) * 8u + r.tab_biased;
+            float next;
+            int count, ge;
+            asm("ld.shared.v2.b32 {%0, %1}, [%2];" : "=f"(next), "=r"(count) : "r"(addr));
+            asm("set.ge.s32.f32 %0, %1, %2;" : "=r"(ge) : "f"(x[i + k]), "f"(next));
+            code[i + k] = count - ge;
+        }
+    }
+}
+
 // Level of a code from the codebook held in registers: lane l keeps
 // cbv = cb[l % 16], and a shuffle reads lane `code`.
 __device__ __forceinline__ float level_of(float cbv, int code) {

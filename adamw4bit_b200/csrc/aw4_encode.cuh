@@ -217,9 +217,11 @@ __device__ __forceinline__ uint32_t encode_fast(const SmemScheme& S, const Schem
     int code[8];
     vdiv_markstein8(x, v, sc, rcp_nr(sc));
     const int floor_code = (MODE != AW4_RTN && zero_floor) ? 1 : 0;
+    int idxs[8];
+    lut_search8(R, x, idxs);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-        const int idx = lut_search(S, R, x[i]);
+        const int idx = idxs[i];
         if (MODE == AW4_RTN) {
             code[i] = idx;  // the dyn4_nz floor is folded into the RTN table
         } else {
