@@ -67,13 +67,17 @@ __device__ __forceinline__ GroupCtx group_ctx(float* warp_scratch, int lane, flo
 // only turn a -0 into +0, and the sums feed max(den, 1e-12) and a quotient
 // whose numerator is a sum of squares, so zero signs never reach a result.
 // Returns (num, den), valid in every lane of the group.
-__device__ __forceinline__ float2 eden_sums(const GroupCtx& g, const float np[8],
-                                            const float dp[8]) {
+// eden_write stores a lane's products; eden_finish (after independent work,
+// if any) reduces them.
+__device__ __forceinline__ void eden_write(const GroupCtx& g, const float np[8],
+                                           const float dp[8]) {
 #pragma unroll
     for (int c = 0; c < 8; ++c) {
         g.tab_num[kEdenCol * c + g.j] = np[c];
         g.tab_den[kEdenCol * c + g.j] = dp[c];
     }
+}
+__device__ __forceinline__ float2 eden_finish(const GroupCtx& g) {
     __syncwarp();
     // lanes 0-7: numerator column j; lanes 8-15: denominator column j - 8
     const float4* col = reinterpret_cast<const float4*>(g.rd);
@@ -108,6 +112,11 @@ __device__ __forceinline__ float2 eden_sums(const GroupCtx& g, const float np[8]
     float num, den;
     upk2(ch, num, den);
     return make_float2(num, den);
+}
+__device__ __forceinline__ float2 eden_sums(const GroupCtx& g, const float np[8],
+                                            const float dp[8]) {
+    eden_write(g, np, dp);
+    return eden_finish(g);
 }
 
 // Encodes the group's block.  v: this lane's 8 working values; amax: their
@@ -203,12 +212,15 @@ __device__ __forceinline__ uint32_t encode_block(const SmemScheme& S, const Sche
 // encode_block for a warp whose blocks all meet the fast preconditions (the
 // caller has voted): a finite scale sc = max(absmax, 1e-12) <= 2^26, and, for
 // SR or EDEN, no nonzero value below 2^-100.  The same results as
-// encode_block, without its per-lane branches.
+// encode_block, without its per-lane branches.  It runs in two parts so a
+// caller can put independent work between them: encode_fast_codes returns the
+// packed codes and, with EDEN, leaves the products in the group's tables;
+// encode_fast_scale then returns the block scale to store.
 template <int MODE>
-__device__ __forceinline__ uint32_t encode_fast(const SmemScheme& S, const SchemeRegs& R,
-                                                const GroupCtx& g, const float v[8], float sc,
-                                                const float u[8], int zero_floor, int eden,
-                                                float sr_bias, float sr_eps, float* scale_out) {
+__device__ __forceinline__ uint32_t encode_fast_codes(const SmemScheme& S, const SchemeRegs& R,
+                                                      const GroupCtx& g, const float v[8],
+                                                      float sc, const float u[8], int zero_floor,
+                                                      int eden, float sr_bias, float sr_eps) {
     if (MODE == AW4_SR_UPDATE) {
         g.levels[g.j] = precond(sc, S.cb[g.j], sr_bias, sr_eps);
         __syncwarp();
@@ -233,26 +245,39 @@ __device__ __forceinline__ uint32_t encode_fast(const SmemScheme& S, const Schem
         }
     }
     if (MODE == AW4_SR_UPDATE) __syncwarp();  // level table reused by the next block
-    float s = sc;
     if (eden) {
         float q[8], np[8], dp[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) q[i] = level_of(R.cbv, code[i]);
         vmul8(np, x, x);
         vmul8(dp, x, q);
-        const float2 nd = eden_sums(g, np, dp);
-        // finite sums here: the divisor lies in [1e-12, 128]
-        const float dd = max_nan(nd.y, kScaleFloor);
-        const bool ok = nd.x == 0.0f || nd.x >= kMarksteinMinNumerator;
-        const float ratio = __all_sync(0xffffffffu, ok) ? div_markstein(nd.x, dd, rcp_nr(dd))
-                                                        : fdiv(nd.x, dd);
-        s = fmul(sc, ratio);
+        eden_write(g, np, dp);
     }
-    *scale_out = s;
     uint32_t packed = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) packed += (uint32_t)code[i] << (4 * i);   // disjoint nibbles
     return packed;
+}
+
+__device__ __forceinline__ float encode_fast_scale(const GroupCtx& g, float sc, int eden) {
+    if (!eden) return sc;
+    const float2 nd = eden_finish(g);
+    // finite sums here: the divisor lies in [1e-12, 128]
+    const float dd = max_nan(nd.y, kScaleFloor);
+    const bool ok = nd.x == 0.0f || nd.x >= kMarksteinMinNumerator;
+    const float ratio = __all_sync(0xffffffffu, ok) ? div_markstein(nd.x, dd, rcp_nr(dd))
+                                                    : fdiv(nd.x, dd);
+    return fmul(sc, ratio);
+}
+
+template <int MODE>
+__device__ __forceinline__ uint32_t encode_fast(const SmemScheme& S, const SchemeRegs& R,
+                                                const GroupCtx& g, const float v[8], float sc,
+                                                const float u[8], int zero_floor, int eden,
+                                                float sr_bias, float sr_eps, float* scale_out) {
+    const uint32_t c = encode_fast_codes<MODE>(S, R, g, v, sc, u, zero_floor, eden, sr_bias, sr_eps);
+    *scale_out = encode_fast_scale(g, sc, eden);
+    return c;
 }
 
 }  // namespace aw4
