@@ -21,7 +21,7 @@ F32, BF16, F16 = 0, 1, 2
 RTN, SR_VALUE, SR_UPDATE = 0, 1, 2
 BLOCK = 128
 LUT_BINS = 1024
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 DTYPE_CODES = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}
 
@@ -59,6 +59,7 @@ class QTensor(ctypes.Structure):
         ("numel", ctypes.c_int64), ("elem_offset", ctypes.c_int64),
         ("ordinal", ctypes.c_uint32), ("hyper", ctypes.c_int32),
         ("param_copy", ctypes.c_void_p),
+        ("copy_multicast", ctypes.c_int32), ("pad", ctypes.c_int32),
     ]
 
 

@@ -57,7 +57,7 @@ struct KDesc {
     int32_t nblocks;
     int32_t tile_begin;
     uint32_t ordinal;
-    int32_t pad;
+    int32_t pc_multicast;   // pc is an NVLink multicast address (multimem stores)
 };
 
 // One hyper-parameter set as the kernel reads it: the caller's aw4_hyper plus
@@ -158,6 +158,22 @@ __device__ __forceinline__ void update_ieee(float q[8], const float m1[8], const
     }
 }
 
+// The BF16 model copy of 8 updated values: a plain store, or, for a ZeRO-1
+// model in symmetric memory, one multimem store to the NVLink multicast
+// address, which NVSwitch delivers to every rank's replica.
+__device__ __forceinline__ void store_model_copy(const KDesc& D, int64_t e0, const float p[8]) {
+    if (!D.pc_multicast) {
+        Elem<AW4_BF16>::store8(D.pc, e0, p);
+        return;
+    }
+    const uint32_t w0 = pack_bf16x2(p[0], p[1]), w1 = pack_bf16x2(p[2], p[3]);
+    const uint32_t w2 = pack_bf16x2(p[4], p[5]), w3 = pack_bf16x2(p[6], p[7]);
+    uint16_t* dst = static_cast<uint16_t*>(D.pc) + e0;
+    asm volatile("multimem.st.relaxed.sys.global.v4.bf16x2 [%0], {%1, %2, %3, %4};" ::"l"(dst),
+                 "r"(w0), "r"(w1), "r"(w2), "r"(w3)
+                 : "memory");
+}
+
 // SR uniforms of 8 values: the test-hook draws buffer when given, else the
 // in-kernel Philox stream of the moment.
 __device__ __forceinline__ void load_uniforms(float u[8], const float* draws, uint64_t key,
@@ -247,7 +263,7 @@ step_kernel(const __grid_constant__ StepLaunch L) {
                 for (int i = 0; i < 8; ++i) p[i] = Elem<PT>::round(p[i]);
                 vadd8(p, q, p, one);                 // p.addcdiv_(m1, den, -lr/bc1)
                 Elem<PT>::store8(D.param, e0, p);
-                if (D.pc != nullptr) Elem<AW4_BF16>::store8(D.pc, e0, p);   // model copy
+                if (D.pc != nullptr) store_model_copy(D, e0, p);
                 if (M1 != AW4_RTN) load_uniforms(u, D.d1, H.m1_key, H, D, e0, true);
                 float ns1, ns2;
                 const uint32_t c1 =
@@ -276,7 +292,7 @@ step_kernel(const __grid_constant__ StepLaunch L) {
             vadd8(p, q, p, one);                     // p.addcdiv_(m1, den, -lr/bc1)
             if (active) {
                 Elem<PT>::store8(D.param, e0, p);
-                if (D.pc != nullptr) Elem<AW4_BF16>::store8(D.pc, e0, p);   // model copy
+                if (D.pc != nullptr) store_model_copy(D, e0, p);
             }
 
             // re-encode m1 (adamw.py:764-771)
@@ -568,6 +584,7 @@ extern "C" int32_t aw4_step_quantized(const aw4_scheme* m1, const aw4_scheme* m2
                 d.d1 = t.m1_draws;
                 d.d2 = t.m2_draws;
                 d.pc = t.param_copy;
+                d.pc_multicast = (t.param_copy && t.copy_multicast) ? 1 : 0;
                 d.elem_offset = t.elem_offset;
                 d.nblocks = (int32_t)(t.numel / AW4_BLOCK);
                 d.tile_begin = L->n_tiles;

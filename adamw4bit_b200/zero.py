@@ -17,6 +17,13 @@ keeps FP32 master weights for the elements it owns only: the fused kernel
 updates the masters and writes bf16(master) into the model in the same pass,
 and the all-gather moves the BF16 model (2 bytes per value instead of 4).
 
+With ``gather="multicast"`` (BF16 model only) there is no separate
+all-gather: the model lives in symmetric memory bound to an NVSwitch
+multicast object, and the update kernel writes each new BF16 value once to
+the multicast address (``multimem`` stores), which delivers it to every
+rank's replica while the kernel runs.  A symmetric-memory barrier ends the
+step.  Without multicast support the optimizer falls back to NCCL.
+
 Ownership is block-cyclic over ``rounds`` rounds: round i covers the flat
 range [i*W*c, (i+1)*W*c) and rank r owns its r-th c-element slice, so each
 round's all-gather writes one contiguous range and can run while the kernel
@@ -42,6 +49,23 @@ _RECIPES = {"ze-eden": ("nf4", "dyn4_nz", True), "zip-sr": ("nf4", "dyn4_upd_sr_
 _M1_OFFSET = 0x1A2B3C4D
 _M2_OFFSET = 0x5E6F7789
 _MAX_SEED = (1 << 63) - 1
+
+
+def _multicast_buffer(n: int, dtype, dev, group):
+    """A flat model buffer in symmetric memory with an NVSwitch multicast
+    address, or (None, None, 0) when the platform offers no multicast."""
+    try:
+        import torch.distributed._symmetric_memory as symm_mem
+        if symm_mem.get_backend(dev) is None:
+            symm_mem.set_backend("CUDA")
+        buf = symm_mem.empty(n, dtype=dtype, device=dev)
+        handle = symm_mem.rendezvous(buf, group if group is not None else dist.group.WORLD)
+        mc = int(handle.multicast_ptr)
+    except (RuntimeError, AttributeError, TypeError):
+        return None, None, 0
+    if not mc:
+        return None, None, 0
+    return buf, handle, mc
 
 
 class ShardPlan:
@@ -102,12 +126,16 @@ class ZeRO1AdamW4Bit:
         reserve_sms: SMs the update grid leaves to the concurrent all-gather.
         master_weights: the parameters are a BF16 model; keep FP32 master
             weights for the owned elements and gather the BF16 model.
+        gather: ``"nccl"`` (all-gather on a side stream) or ``"multicast"``
+            (the update kernel writes every replica through NVSwitch; needs
+            ``master_weights`` and a process group of 2+ ranks).
     """
 
     def __init__(self, params, *, recipe: str = "ze-eden", lr: float = 1e-3,
                  betas=(0.9, 0.95), eps: float = 1e-8, weight_decay: float = 0.1,
                  process_group=None, rounds: int = 4, quant_rng_seed: int = 0,
-                 reserve_sms: int = 16, master_weights: bool = False):
+                 reserve_sms: int = 16, master_weights: bool = False,
+                 gather: str = "nccl"):
         self.params = [p for p in params]
         if not self.params:
             raise ValueError("ZeRO1AdamW4Bit needs parameters")
@@ -129,14 +157,29 @@ class ZeRO1AdamW4Bit:
             raise ValueError("master_weights=True needs BF16 parameters (the model copy)")
         self.master_weights = master_weights
         self.device, self.dtype = dev, dtype
+        self.quant_rng_seed = quant_rng_seed
         self.keys = ((quant_rng_seed + _M1_OFFSET) % _MAX_SEED,
                      (quant_rng_seed + _M2_OFFSET) % _MAX_SEED)
         W = self.world
         plan = ShardPlan([p.numel() for p in self.params], W, self.rank, rounds)
         self.plan = plan
         self.chunk, self.padded, self.total = plan.chunk, plan.padded, plan.total
+        if gather not in ("nccl", "multicast"):
+            raise ValueError(f"unknown gather mode {gather!r}")
+        if gather == "multicast" and not master_weights:
+            raise ValueError('gather="multicast" needs master_weights=True (a BF16 model)')
+        self.symm = None
+        self.mc_base = 0
+        flat = None
+        if gather == "multicast" and W > 1:
+            flat, self.symm, self.mc_base = _multicast_buffer(plan.padded, dtype, dev,
+                                                              self.group)
+        self.gather_mode = "multicast" if self.mc_base else "nccl"
         # re-home parameters into one flat buffer (zero padding at the end)
-        flat = torch.zeros(plan.padded, dtype=dtype, device=dev)
+        if flat is None:
+            flat = torch.zeros(plan.padded, dtype=dtype, device=dev)
+        else:
+            flat.zero_()
         for p, off in zip(self.params, plan.starts):
             n = p.numel()
             flat[off:off + n].copy_(p.detach().reshape(-1))
@@ -165,11 +208,14 @@ class ZeRO1AdamW4Bit:
                     "aw4_init_zero_state")
         self.step_count = 0
         self.segments = plan.segments
-        self.gather_stream = torch.cuda.Stream(dev) if W > 1 else None
+        nccl = W > 1 and self.gather_mode == "nccl"
+        self.gather_stream = torch.cuda.Stream(dev) if nccl else None
         # With a concurrent all-gather, leave `reserve_sms` SMs free so NCCL's
         # kernels can run beside the persistent update grid (4 CTAs per SM).
         sms = torch.cuda.get_device_properties(dev).multi_processor_count
-        self.max_ctas = max(1, (sms - reserve_sms) * 4) if W > 1 else 0
+        self.max_ctas = max(1, (sms - reserve_sms) * 4) if nccl else 0
+        if self.symm is not None:
+            self.symm.barrier(channel=0)   # every replica holds the initial model
         self.launch_timings: list | None = None
 
     @torch.no_grad()
@@ -195,6 +241,10 @@ class ZeRO1AdamW4Bit:
             for ti, s, n, so in segs:
                 p, g = self.params[ti], grads[ti]
                 model = p.data_ptr() + s * esz_p
+                multicast = 0
+                if self.gather_mode == "multicast":   # every rank's replica, via NVSwitch
+                    model = self.mc_base + (self.plan.starts[ti] + s) * esz_p
+                    multicast = 1
                 if self.master_weights:   # update the FP32 master, write the BF16 model
                     target, copy = self.master.data_ptr() + so * 4, model
                 else:
@@ -203,7 +253,7 @@ class ZeRO1AdamW4Bit:
                     target, g.data_ptr() + s * g.element_size(),
                     self.m1_codes.data_ptr() + so // 2, self.m1_scales.data_ptr() + (so // 128) * 4,
                     self.m2_codes.data_ptr() + so // 2, self.m2_scales.data_ptr() + (so // 128) * 4,
-                    None, None, n, s, ti, 0, copy))
+                    None, None, n, s, ti, 0, copy, multicast))
             if descs:
                 arr = (N.QTensor * len(descs))(*descs)
                 if self.launch_timings is not None:
@@ -217,15 +267,150 @@ class ZeRO1AdamW4Bit:
                 if self.launch_timings is not None:
                     e1.record(cur)
                     self.launch_timings.append((e0, e1, sum(d.numel for d in descs), pdt, gdt))
-            if W > 1:
+            if W > 1 and self.gather_mode == "nccl":
                 base = r * W * self.chunk
                 region = self.flat[base:base + W * self.chunk]
                 mine = region[self.rank * self.chunk:(self.rank + 1) * self.chunk]
                 self.gather_stream.wait_stream(cur)
                 with torch.cuda.stream(self.gather_stream):
                     dist.all_gather_into_tensor(region, mine, group=self.group)
-        if W > 1:
+        if W > 1 and self.gather_mode == "nccl":
             cur.wait_stream(self.gather_stream)
+        elif self.symm is not None:
+            # every rank's multimem stores are in every replica once all
+            # ranks' update kernels have completed
+            self.symm.barrier(channel=0)
 
     def owned_numel(self) -> int:
         return self.plan.owned_numel()
+
+    # ------------------------------------------------------------ checkpoints
+    _SHARD_KIND = "zero1-shard"
+
+    def _shard_buffers(self) -> dict:
+        bufs = {"m1_codes": self.m1_codes, "m1_scales": self.m1_scales,
+                "m2_codes": self.m2_codes, "m2_scales": self.m2_scales}
+        if self.master is not None:
+            bufs["master"] = self.master
+        return bufs
+
+    def _config(self) -> dict:
+        return {"world": self.world, "rounds": self.plan.rounds,
+                "sizes": list(self.plan.sizes), "recipe": (self.m1, self.m2, self.eden),
+                "master_weights": self.master_weights}
+
+    def state_dict(self, consolidated: bool = False) -> dict:
+        """Optimizer state for a checkpoint.
+
+        Default: this rank's shard (its packed codes, block scales and FP32
+        masters, as device tensors) plus the sharding it depends on; every rank
+        saves its own and loads it back into the same layout.
+
+        ``consolidated=True`` (a collective: every rank must call it): the
+        whole state in the per-parameter layout of the single-GPU
+        optimizer's ``state_dict`` (``m1_code`` / ``m1_quant_state`` / ...,
+        adamw.py:330-336), on the CPU, so a ZeRO run can resume on one GPU and
+        the other way round; FP32 masters, if any, under ``"master_weights"``.
+        """
+        group = {"lr": self.lr, "betas": self.betas, "eps": self.eps,
+                 "weight_decay": self.wd}
+        if not consolidated:
+            return {"kind": self._SHARD_KIND, "rank": self.rank, "step": self.step_count,
+                    "config": self._config(), "param_group": group,
+                    "buffers": {k: v.detach().clone() for k, v in self._shard_buffers().items()}}
+        glob = self._gather_state()
+        from .optimizer import ZEEDENAdamW4Bit, ZIPSRAdamW4Bit
+        cls = ZEEDENAdamW4Bit if self.eden else ZIPSRAdamW4Bit
+        template = cls([torch.nn.Parameter(torch.zeros(4096))],
+                       quant_rng_seed=None if self.eden else self.quant_rng_seed)
+        defaults = {k: v for k, v in template.param_groups[0].items() if k != "params"}
+        defaults.update(group)
+        state, masters = {}, {}
+        for i, (p, s0) in enumerate(zip(self.params, self.plan.starts)):
+            n = p.numel()
+            entry = {"step": self.step_count}
+            for m in ("m1", "m2"):
+                entry[f"{m}_code"] = glob[f"{m}_codes"][s0 // 2:(s0 + n) // 2].clone()
+                entry[f"{m}_quant_state"] = {
+                    "absmax": glob[f"{m}_scales"][s0 // 128:(s0 + n) // 128].clone(),
+                    "shape": p.shape, "dtype": torch.float32, "blocksize": 128, "packed": True}
+            state[i] = entry
+            if "master" in glob:
+                masters[i] = glob["master"][s0:s0 + n].clone().view(p.shape)
+        result = {"state": state,
+                  "param_groups": [{**defaults, "params": list(range(len(self.params)))}]}
+        if not self.eden:
+            result["_quant_rng_state"] = {"version": 2, "seed": self.quant_rng_seed,
+                                          "stream": "philox4x32-10"}
+        if masters:
+            result["master_weights"] = masters
+        return result
+
+    def _gather_state(self) -> dict:
+        """All ranks' state buffers in the global flat element order, on the CPU."""
+        W, R, c = self.world, self.plan.rounds, self.chunk
+        units = {"m1_codes": c // 2, "m2_codes": c // 2, "m1_scales": c // 128,
+                 "m2_scales": c // 128, "master": c}
+        totals = {"m1_codes": self.total // 2, "m2_codes": self.total // 2,
+                  "m1_scales": self.total // 128, "m2_scales": self.total // 128,
+                  "master": self.total}
+        out = {}
+        for name, buf in self._shard_buffers().items():
+            if W > 1:
+                g = torch.empty((W,) + tuple(buf.shape), dtype=buf.dtype, device=buf.device)
+                dist.all_gather_into_tensor(g.view(-1), buf.contiguous(), group=self.group)
+            else:
+                g = buf.unsqueeze(0)
+            # rank k's round-r chunk is global chunk r*W + k
+            g = g.view(W, R, units[name]).transpose(0, 1).reshape(-1)
+            out[name] = g[:totals[name]].cpu()
+        return out
+
+    def load_state_dict(self, state_dict: dict) -> None:
+        """Restore a shard dict saved by this rank (same sharding) or a
+        consolidated / single-GPU optimizer state dict (re-sharded here)."""
+        if state_dict.get("kind") == self._SHARD_KIND:
+            if state_dict["config"] != self._config() or state_dict["rank"] != self.rank:
+                raise ValueError("shard checkpoint was saved with a different sharding "
+                                 "(world, rounds, sizes, recipe) or rank")
+            for k, v in self._shard_buffers().items():
+                v.copy_(state_dict["buffers"][k])
+            self.step_count = int(state_dict["step"])
+            g = state_dict["param_group"]
+            self.lr, self.betas, self.eps, self.wd = g["lr"], tuple(g["betas"]), g["eps"], g["weight_decay"]
+            return
+        states = state_dict["state"]
+        groups = state_dict["param_groups"]
+        order = [i for grp in groups for i in grp["params"]]
+        if len(order) != len(self.params):
+            raise ValueError("state dict holds a different number of parameters")
+        masters = state_dict.get("master_weights", {})
+        if self.master_weights and not masters:
+            raise ValueError("master_weights=True needs FP32 masters in the state dict")
+        steps = set()
+        for ti, index in enumerate(order):
+            st = states.get(index)
+            if not st or "m1_code" not in st:
+                raise ValueError(f"parameter {ti}: no packed 4-bit state in the state dict")
+            steps.add(int(st["step"]))
+            for segs in self.segments:
+                for sti, s0, n, so in segs:
+                    if sti != ti:
+                        continue
+                    for m in ("m1", "m2"):
+                        codes = getattr(self, f"{m}_codes")
+                        scales = getattr(self, f"{m}_scales")
+                        qs = st[f"{m}_quant_state"]
+                        absmax = qs["absmax"] if isinstance(qs, dict) else qs.absmax
+                        codes[so // 2:(so + n) // 2].copy_(
+                            st[f"{m}_code"].reshape(-1)[s0 // 2:(s0 + n) // 2])
+                        scales[so // 128:(so + n) // 128].copy_(
+                            absmax.reshape(-1)[s0 // 128:(s0 + n) // 128])
+                    if self.master is not None:
+                        self.master[so:so + n].copy_(
+                            masters[index].reshape(-1)[s0:s0 + n].to(torch.float32))
+        if len(steps) != 1:
+            raise ValueError("parameters are at different steps")
+        self.step_count = steps.pop()
+        g = groups[0]
+        self.lr, self.betas, self.eps, self.wd = g["lr"], tuple(g["betas"]), g["eps"], g["weight_decay"]

@@ -298,7 +298,7 @@ def run_ours(args, rank, world, local):
     if args.values:
         shapes = [(args.values,)]   # single-tensor case (profiling)
     total = sum(int(torch.Size(s).numel()) for s in shapes)
-    master = world > 1 and args.gather == "bf16"
+    master = world > 1 and args.gather in ("bf16", "multicast")
     params, grads = make_workload(dev, shapes,
                                   param_dtype=torch.bfloat16 if master else torch.float32)
     if world == 1:
@@ -309,7 +309,8 @@ def run_ours(args, rank, world, local):
         # FP32 masters sharded over the ranks; with --gather bf16 the model is
         # BF16 (written by the update kernel) and the all-gather moves 2 B/value
         opt = ZeRO1AdamW4Bit(params, recipe="ze-eden", rounds=args.rounds,
-                             master_weights=master, reserve_sms=args.reserve_sms)
+                             master_weights=master, reserve_sms=args.reserve_sms,
+                             gather="multicast" if args.gather == "multicast" else "nccl")
         step_fn = opt.step
         updated_per_rank = opt.owned_numel()
     b_per_elem = B_PER_ELEM + (2 if master else 0)   # + the BF16 model copy write
@@ -378,7 +379,8 @@ def run_ours(args, rank, world, local):
                            "param_dtype": "fp32 master + bf16 model copy" if master else "fp32",
                            "grad_dtype": "bf16", "recipe": "ZE-EDEN",
                            "parallelism": "single GPU" if world == 1 else
-                           f"zero1-dp{world}, {'bf16 model' if master else 'fp32'} all-gather",
+                           f"zero1-dp{world}, {'bf16 model' if master else 'fp32'} gather "
+                           f"({getattr(opt, 'gather_mode', 'nccl')})",
                            "l2": "no flush: 56 GB working set >> 126 MB L2"},
                 "roofline": roofline,
                 "update_only": {"values_per_rank": updated_per_rank,
@@ -471,9 +473,11 @@ def main():
     ap.add_argument("--rounds", type=int, default=4, help="ZeRO-1 gather rounds")
     ap.add_argument("--reserve-sms", type=int, default=16,
                     help="N>1: SMs the update grid leaves to the concurrent all-gather")
-    ap.add_argument("--gather", choices=["bf16", "fp32"], default="bf16",
-                    help="N>1: all-gather a BF16 model copy of the FP32 masters (default) or "
-                         "the FP32 parameters themselves")
+    ap.add_argument("--gather", choices=["multicast", "bf16", "fp32"], default="bf16",
+                    help="N>1: the BF16 model copy of the FP32 masters written to every "
+                         "replica by the update kernel through NVSwitch multicast, or "
+                         "all-gathered by NCCL (bf16, default), or the FP32 parameters "
+                         "all-gathered by NCCL")
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--cpu-sample", type=int, default=1 << 27,
                     help="values in the CPU-oracle sample (0: skip)")

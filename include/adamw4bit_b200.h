@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define AW4_ABI_VERSION 2
+#define AW4_ABI_VERSION 3
 #define AW4_BLOCK 128          /* elements per quantization block (4-bit default) */
 #define AW4_LUT_BINS 1024      /* maximum uniform bins over [-1, 1] for the rounding search */
 
@@ -106,6 +106,11 @@ typedef struct aw4_qtensor {
     void* param_copy;              /* NULL, or numel BF16 values that receive bf16(updated
                                     * param): the model copy of FP32 master parameters
                                     * (16-byte aligned; FP32 params only) */
+    int32_t copy_multicast;        /* nonzero: param_copy is an NVLink multicast address
+                                    * (an NVSwitch multicast object bound on every rank);
+                                    * the copy is written with multimem stores and lands
+                                    * in every rank's replica */
+    int32_t pad;
 } aw4_qtensor;
 
 /* One tensor with FP32 moments (numel arbitrary). */

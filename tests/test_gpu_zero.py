@@ -24,7 +24,7 @@ def _make(dev, seed=0):
     return params, grads
 
 
-def _worker(rank, world, port, recipe, rounds, q, master=False):
+def _worker(rank, world, port, recipe, rounds, q, master=False, gather="nccl"):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     import datetime
 
@@ -45,7 +45,10 @@ def _worker(rank, world, port, recipe, rounds, q, master=False):
         for p in params:
             p.grad_dtype = None
         opt = ZeRO1AdamW4Bit(params, recipe=recipe, rounds=rounds, quant_rng_seed=9,
-                             master_weights=master)
+                             master_weights=master, gather=gather)
+        if opt.gather_mode != gather:
+            q.put((rank, True, "skip: no NVSwitch multicast on this platform"))
+            return
         for step_grads in grads:
             for p, g in zip(params, step_grads):
                 p.grad = g
@@ -63,6 +66,18 @@ def _worker(rank, world, port, recipe, rounds, q, master=False):
                 p.grad = g
             single.step()
         torch.cuda.synchronize()
+        # the consolidated checkpoint gathers every rank's shard: it must hold
+        # the single-GPU optimizer's codes and scales bit for bit
+        cons = opt.state_dict(consolidated=True)
+        sref = single.state_dict()
+        for i in sref["state"]:
+            for key in ("m1_code", "m2_code"):
+                if not torch.equal(cons["state"][i][key], sref["state"][i][key].cpu()):
+                    raise AssertionError(f"consolidated {key} of parameter {i} differs")
+            for key in ("m1_quant_state", "m2_quant_state"):
+                if not torch.equal(cons["state"][i][key]["absmax"].view(torch.int32),
+                                   sref["state"][i][key]["absmax"].cpu().view(torch.int32)):
+                    raise AssertionError(f"consolidated {key} of parameter {i} differs")
         if master:
             # the gathered BF16 model is bf16(the unsharded FP32 params) everywhere,
             # and this rank's FP32 masters equal the unsharded params it owns
@@ -77,29 +92,38 @@ def _worker(rank, world, port, recipe, rounds, q, master=False):
         else:
             ok = all(torch.equal(a.detach().view(torch.int32), b.detach().view(torch.int32))
                      for a, b in zip(params, ref))
+        # both ranks finish all device work (multicast stores included) before
+        # either exits
+        torch.cuda.synchronize()
+        dist.barrier()
         q.put((rank, ok, None))
     except Exception as e:  # report to the parent instead of hanging it
         q.put((rank, False, repr(e)))
     finally:
         if dist.is_initialized():
+            torch.cuda.synchronize()
             dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("recipe,rounds,master", [("ze-eden", 1, False), ("ze-eden", 3, False),
-                                                  ("zip-sr", 2, False), ("ze-eden", 2, True)])
-def test_zero1_two_gpus_matches_single_gpu_bit_exact(recipe, rounds, master):
+@pytest.mark.parametrize("recipe,rounds,master,gather", [
+    ("ze-eden", 1, False, "nccl"), ("ze-eden", 3, False, "nccl"), ("zip-sr", 2, False, "nccl"),
+    ("ze-eden", 2, True, "nccl"), ("ze-eden", 2, True, "multicast"),
+    ("zip-sr", 3, True, "multicast")])
+def test_zero1_two_gpus_matches_single_gpu_bit_exact(recipe, rounds, master, gather):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = 29600 + (os.getpid() % 500) + (7 if master else 0)
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, recipe, rounds, q, master))
+    port = 29600 + (os.getpid() % 400) + (7 if master else 0) + (13 if gather != "nccl" else 0)
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, recipe, rounds, q, master, gather))
              for r in range(2)]
     for p in procs:
         p.start()
     results = [q.get(timeout=300) for _ in procs]
     for p in procs:
         p.join(timeout=60)
+    if all(msg and str(msg).startswith("skip") for _, _, msg in results):
+        pytest.skip(results[0][2])
     assert all(ok for _, ok, _ in results), results
 
 
@@ -130,3 +154,79 @@ def test_zero1_master_weights_on_one_gpu_matches_fp32_step():
         for ti, s0, n, so in segs:
             want = fp32[ti].detach().reshape(-1)[s0:s0 + n]
             assert torch.equal(opt.master[so:so + n].view(torch.int32), want.view(torch.int32))
+
+
+def _run(opt, params, grads):
+    for step_grads in grads:
+        for p, g in zip(params, step_grads):
+            p.grad = g
+        opt.step()
+
+
+def test_zero1_consolidated_state_dict_resumes_on_the_single_gpu_optimizer():
+    """ZeRO-1 (one rank) -> consolidated state dict -> the single-GPU
+    optimizer continues bit-identically, and the other way round."""
+    from adamw4bit_b200 import ZEEDENAdamW4Bit
+    from adamw4bit_b200.zero import ZeRO1AdamW4Bit
+    dev = torch.device("cuda", 0)
+    vals, grads = _make(dev, seed=5)
+    za = [torch.nn.Parameter(v.clone()) for v in vals]
+    sa = [torch.nn.Parameter(v.clone()) for v in vals]
+    for p in za + sa:
+        p.grad_dtype = None
+    zopt = ZeRO1AdamW4Bit(za, recipe="ze-eden", rounds=3)
+    sopt = ZEEDENAdamW4Bit(sa)
+    _run(zopt, za, grads[:2])
+    _run(sopt, sa, grads[:2])
+    sd = zopt.state_dict(consolidated=True)
+    ref = sopt.state_dict()
+    for i in ref["state"]:
+        for key in ("m1_code", "m2_code"):
+            assert torch.equal(sd["state"][i][key], ref["state"][i][key].cpu()), (i, key)
+        for key in ("m1_quant_state", "m2_quant_state"):
+            assert torch.equal(sd["state"][i][key]["absmax"].view(torch.int32),
+                               ref["state"][i][key]["absmax"].cpu().view(torch.int32)), (i, key)
+    # ZeRO -> single GPU
+    sb = [torch.nn.Parameter(p.detach().clone()) for p in za]
+    for p in sb:
+        p.grad_dtype = None
+    sopt_b = ZEEDENAdamW4Bit(sb)
+    sopt_b.load_state_dict(sd)
+    # single GPU -> ZeRO
+    zb = [torch.nn.Parameter(p.detach().clone()) for p in sa]
+    for p in zb:
+        p.grad_dtype = None
+    zopt_b = ZeRO1AdamW4Bit(zb, recipe="ze-eden", rounds=2)
+    zopt_b.load_state_dict(ref)
+    _run(zopt, za, grads[2:])
+    _run(sopt_b, sb, grads[2:])
+    _run(zopt_b, zb, grads[2:])
+    torch.cuda.synchronize()
+    for a, b, c in zip(za, sb, zb):
+        assert torch.equal(a.view(torch.int32), b.view(torch.int32))
+        assert torch.equal(a.view(torch.int32), c.view(torch.int32))
+
+
+def test_zero1_shard_state_dict_round_trip_with_master_weights():
+    from adamw4bit_b200.zero import ZeRO1AdamW4Bit
+    dev = torch.device("cuda", 0)
+    vals, grads = _make(dev, seed=6)
+    a = [torch.nn.Parameter(v.to(torch.bfloat16)) for v in vals]
+    b = [torch.nn.Parameter(v.to(torch.bfloat16)) for v in vals]
+    opt_a = ZeRO1AdamW4Bit(a, recipe="zip-sr", rounds=2, master_weights=True, quant_rng_seed=4)
+    _run(opt_a, a, grads[:2])
+    sd = opt_a.state_dict()
+    opt_b = ZeRO1AdamW4Bit(b, recipe="zip-sr", rounds=2, master_weights=True, quant_rng_seed=4)
+    for pa, pb in zip(a, b):
+        pb.data.copy_(pa.data)
+    opt_b.load_state_dict(sd)
+    _run(opt_a, a, grads[2:])
+    _run(opt_b, b, grads[2:])
+    torch.cuda.synchronize()
+    for pa, pb in zip(a, b):
+        assert torch.equal(pa.view(torch.int16), pb.view(torch.int16))
+    assert torch.equal(opt_a.master.view(torch.int32), opt_b.master.view(torch.int32))
+    bad = ZeRO1AdamW4Bit([torch.nn.Parameter(v.to(torch.bfloat16)) for v in vals], recipe="zip-sr",
+                         rounds=3, master_weights=True, quant_rng_seed=4)
+    with pytest.raises(ValueError, match="different sharding"):
+        bad.load_state_dict(sd)
