@@ -58,8 +58,9 @@ quantize_kernel(const __grid_constant__ aw4_scheme scheme, int eden, const float
         // codec tests cover both encoders)
         float s;
         const float amax = lane_absmax(v);
-        const float sc = max_nan(group_max16(amax), kScaleFloor);
-        bool ok = sc <= kMarksteinMaxDivisor;   // false for NaN / inf
+        const float gmax = group_max16(amax);
+        const float sc = max_nan(gmax, kScaleFloor);
+        bool ok = sc <= kMarksteinMaxDivisor && (gmax >= kScaleFloor || !eden);   // false for NaN / inf
         if (MODE != AW4_RTN || eden) ok = none_tiny_warp(v, ok);
         const uint32_t c = __all_sync(0xffffffffu, ok)
                                ? encode_fast<MODE>(S, R, g, v, sc, u, scheme.zero_floor, eden,

@@ -210,8 +210,8 @@ __device__ __forceinline__ uint32_t encode_block(const SmemScheme& S, const Sche
 }
 
 // encode_block for a warp whose blocks all meet the fast preconditions (the
-// caller has voted): a finite scale sc = max(absmax, 1e-12) <= 2^26, and, for
-// SR or EDEN, no nonzero value below 2^-100.  The same results as
+// caller has voted): a finite scale sc = max(absmax, 1e-12) <= 2^26; for SR
+// or EDEN, no nonzero value below 2^-100; for EDEN, absmax >= 1e-12.  The same results as
 // encode_block, without its per-lane branches.  It runs in two parts so a
 // caller can put independent work between them: encode_fast_codes returns the
 // packed codes and, with EDEN, leaves the products in the group's tables;
@@ -259,15 +259,15 @@ __device__ __forceinline__ uint32_t encode_fast_codes(const SmemScheme& S, const
     return packed;
 }
 
+// With EDEN the fast path also requires absmax >= 1e-12, so sc is the block's
+// absmax and its largest element normalises to exactly +-1, a codebook level
+// of every supported scheme (coded to itself by RTN and by both SR rules).
+// Both sums then hold a term equal to 1 among non-negative terms: they lie in
+// [1, 128], max(den, 1e-12) is den, and Markstein's preconditions hold.
 __device__ __forceinline__ float encode_fast_scale(const GroupCtx& g, float sc, int eden) {
     if (!eden) return sc;
     const float2 nd = eden_finish(g);
-    // finite sums here: the divisor lies in [1e-12, 128]
-    const float dd = max_nan(nd.y, kScaleFloor);
-    const bool ok = nd.x == 0.0f || nd.x >= kMarksteinMinNumerator;
-    const float ratio = __all_sync(0xffffffffu, ok) ? div_markstein(nd.x, dd, rcp_nr(dd))
-                                                    : fdiv(nd.x, dd);
-    return fmul(sc, ratio);
+    return fmul(sc, div_markstein(nd.x, nd.y, rcp_nr(nd.y)));
 }
 
 template <int MODE>

@@ -249,9 +249,11 @@ step_kernel(const __grid_constant__ StepLaunch L) {
             // One warp-uniform decision per sub-block: when every lane meets the
             // fast preconditions the rest runs without per-lane branches.
             const float sc1 = max_nan(group_max16(amax1), kScaleFloor);
-            const float sc2 = max_nan(group_max16(amax2), kScaleFloor);
+            const float gmax2 = group_max16(amax2);
+            const float sc2 = max_nan(gmax2, kScaleFloor);
             bool ok = active && amax1 <= H.m1_fast_max && amax2 <= H.m2_fast_max &&
-                      sc1 <= kMarksteinMaxDivisor && sc2 <= kMarksteinMaxDivisor;
+                      sc1 <= kMarksteinMaxDivisor && sc2 <= kMarksteinMaxDivisor &&
+                      (gmax2 >= kScaleFloor || !L.eden);
             ok = none_tiny_warp(nt, ok);
             if (M1 != AW4_RTN) ok = none_tiny_warp(m1, ok);
             if (M2 != AW4_RTN || L.eden) ok = none_tiny_warp(m2, ok);
