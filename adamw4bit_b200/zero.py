@@ -114,8 +114,10 @@ class ShardPlan:
 
 
 class ZeRO1AdamW4Bit:
-    """Sharded fused step over quantized parameters (every tensor eligible:
-    numel a multiple of 128 and at least 4096).
+    """Sharded fused step over a model's parameters.  Tensors eligible for
+    4-bit state (numel a multiple of 128 and at least 4096, adamw.py:807-811)
+    are sharded; the others keep FP32 moments replicated on every rank, which
+    all run the same FP32-state update (bit-identical replicas, no exchange).
 
     Args:
         params: CUDA parameters of one dtype, all on this rank's device.
@@ -136,9 +138,15 @@ class ZeRO1AdamW4Bit:
                  process_group=None, rounds: int = 4, quant_rng_seed: int = 0,
                  reserve_sms: int = 16, master_weights: bool = False,
                  gather: str = "nccl"):
-        self.params = [p for p in params]
-        if not self.params:
+        self.all_params = [p for p in params]
+        if not self.all_params:
             raise ValueError("ZeRO1AdamW4Bit needs parameters")
+        eligible = [p.numel() >= 4096 and p.numel() % 128 == 0 for p in self.all_params]
+        self.qindex = [i for i, e in enumerate(eligible) if e]        # sharded, 4-bit state
+        self.sindex = [i for i, e in enumerate(eligible) if not e]    # replicated, FP32 state
+        self.params = [self.all_params[i] for i in self.qindex]
+        if not self.params:
+            raise ValueError("ZeRO1AdamW4Bit needs at least one tensor of >= 4096 values")
         self.m1, self.m2, self.eden = _RECIPES[recipe]
         self.lr, self.betas, self.eps, self.wd = lr, betas, eps, weight_decay
         self.group = process_group
@@ -146,13 +154,10 @@ class ZeRO1AdamW4Bit:
         self.rank = dist.get_rank(process_group) if dist.is_initialized() else 0
         dev = self.params[0].device
         dtype = self.params[0].dtype
-        for p in self.params:
+        for p in self.all_params:
             N.require_cuda(p, "ZeRO1AdamW4Bit")
             if p.device != dev or p.dtype != dtype:
                 raise ValueError("all parameters must share one device and dtype")
-            if p.numel() % 128 or p.numel() < 4096:
-                raise NotImplementedError("ZeRO1AdamW4Bit shards quantized tensors only "
-                                          "(numel >= 4096, multiple of 128)")
         if master_weights and dtype != torch.bfloat16:
             raise ValueError("master_weights=True needs BF16 parameters (the model copy)")
         self.master_weights = master_weights
@@ -206,6 +211,15 @@ class ZeRO1AdamW4Bit:
             N.check(N.lib().aw4_init_zero_state(prepared(scheme), int(e), N.ptr(codes),
                                                 N.ptr(scales), n_own, dev.index, stream),
                     "aw4_init_zero_state")
+        # FP32-state tensors, replicated: moments (and masters) per tensor
+        self.small = []
+        for i in self.sindex:
+            p = self.all_params[i]
+            entry = {"m1": torch.zeros(p.numel(), dtype=torch.float32, device=dev),
+                     "m2": torch.zeros(p.numel(), dtype=torch.float32, device=dev)}
+            if master_weights:
+                entry["master"] = p.detach().reshape(-1).float().clone()
+            self.small.append(entry)
         self.step_count = 0
         self.segments = plan.segments
         nccl = W > 1 and self.gather_mode == "nccl"
@@ -232,7 +246,8 @@ class ZeRO1AdamW4Bit:
         pdt = N.DTYPE_CODES[torch.float32 if self.master_weights else self.dtype]
         esz_p = self.flat.element_size()
         grads = [p.grad for p in self.params]
-        if any(g is None for g in grads):
+        if any(g is None for g in grads) or any(self.all_params[i].grad is None
+                                                for i in self.sindex):
             raise RuntimeError("ZeRO1AdamW4Bit.step needs a gradient for every parameter")
         gdt = N.DTYPE_CODES[grads[0].dtype]
         W = self.world
@@ -253,7 +268,9 @@ class ZeRO1AdamW4Bit:
                     target, g.data_ptr() + s * g.element_size(),
                     self.m1_codes.data_ptr() + so // 2, self.m1_scales.data_ptr() + (so // 128) * 4,
                     self.m2_codes.data_ptr() + so // 2, self.m2_scales.data_ptr() + (so // 128) * 4,
-                    None, None, n, s, ti, 0, copy, multicast))
+                    # Philox ordinal: the position among all parameters, as in
+                    # the single-GPU optimizer, so SR draws do not depend on sharding
+                    None, None, n, s, self.qindex[ti], 0, copy, multicast))
             if descs:
                 arr = (N.QTensor * len(descs))(*descs)
                 if self.launch_timings is not None:
@@ -274,12 +291,36 @@ class ZeRO1AdamW4Bit:
                 self.gather_stream.wait_stream(cur)
                 with torch.cuda.stream(self.gather_stream):
                     dist.all_gather_into_tensor(region, mine, group=self.group)
+        self._step_small(harr, cur)
         if W > 1 and self.gather_mode == "nccl":
             cur.wait_stream(self.gather_stream)
         elif self.symm is not None:
             # every rank's multimem stores are in every replica once all
             # ranks' update kernels have completed
             self.symm.barrier(channel=0)
+
+    def _step_small(self, harr, cur) -> None:
+        """The FP32-state update of the small tensors, identical on every rank
+        (adamw.py:807-817); with master weights the BF16 model copy follows."""
+        if not self.small:
+            return
+        dev = self.device
+        pdt = N.DTYPE_CODES[torch.float32 if self.master_weights else self.dtype]
+        gdt = N.DTYPE_CODES[self.all_params[self.sindex[0]].grad.dtype]
+        descs, keep = [], []
+        for i, st in zip(self.sindex, self.small):
+            p = self.all_params[i]
+            target = st["master"] if self.master_weights else p
+            g = p.grad.contiguous()
+            keep.append(g)
+            descs.append(N.FTensor(target.data_ptr(), g.data_ptr(),
+                                   st["m1"].data_ptr(), st["m2"].data_ptr(), p.numel(), 0, 0))
+        arr = (N.FTensor * len(descs))(*descs)
+        N.check(N.lib().aw4_step_fp32_state(pdt, gdt, arr, len(descs), harr, 1, dev.index,
+                                            cur.cuda_stream), "aw4_step_fp32_state")
+        if self.master_weights:
+            for i, st in zip(self.sindex, self.small):
+                self.all_params[i].data.copy_(st["master"].view(self.all_params[i].shape))
 
     def owned_numel(self) -> int:
         return self.plan.owned_numel()
@@ -296,8 +337,9 @@ class ZeRO1AdamW4Bit:
 
     def _config(self) -> dict:
         return {"world": self.world, "rounds": self.plan.rounds,
-                "sizes": list(self.plan.sizes), "recipe": (self.m1, self.m2, self.eden),
-                "master_weights": self.master_weights}
+                "sizes": list(self.plan.sizes), "small": [self.all_params[i].numel()
+                                                          for i in self.sindex],
+                "recipe": (self.m1, self.m2, self.eden), "master_weights": self.master_weights}
 
     def state_dict(self, consolidated: bool = False) -> dict:
         """Optimizer state for a checkpoint.
@@ -317,7 +359,9 @@ class ZeRO1AdamW4Bit:
         if not consolidated:
             return {"kind": self._SHARD_KIND, "rank": self.rank, "step": self.step_count,
                     "config": self._config(), "param_group": group,
-                    "buffers": {k: v.detach().clone() for k, v in self._shard_buffers().items()}}
+                    "buffers": {k: v.detach().clone() for k, v in self._shard_buffers().items()},
+                    "small": [{k: v.detach().clone() for k, v in st.items()}
+                              for st in self.small]}
         glob = self._gather_state()
         from .optimizer import ZEEDENAdamW4Bit, ZIPSRAdamW4Bit
         cls = ZEEDENAdamW4Bit if self.eden else ZIPSRAdamW4Bit
@@ -326,7 +370,8 @@ class ZeRO1AdamW4Bit:
         defaults = {k: v for k, v in template.param_groups[0].items() if k != "params"}
         defaults.update(group)
         state, masters = {}, {}
-        for i, (p, s0) in enumerate(zip(self.params, self.plan.starts)):
+        for ti, (p, s0) in enumerate(zip(self.params, self.plan.starts)):
+            i = self.qindex[ti]
             n = p.numel()
             entry = {"step": self.step_count}
             for m in ("m1", "m2"):
@@ -337,8 +382,14 @@ class ZeRO1AdamW4Bit:
             state[i] = entry
             if "master" in glob:
                 masters[i] = glob["master"][s0:s0 + n].clone().view(p.shape)
+        for i, st in zip(self.sindex, self.small):
+            shape = self.all_params[i].shape
+            state[i] = {"step": self.step_count, "m1": st["m1"].view(shape).cpu().clone(),
+                        "m2": st["m2"].view(shape).cpu().clone()}
+            if "master" in st:
+                masters[i] = st["master"].view(shape).cpu().clone()
         result = {"state": state,
-                  "param_groups": [{**defaults, "params": list(range(len(self.params)))}]}
+                  "param_groups": [{**defaults, "params": list(range(len(self.all_params)))}]}
         if not self.eden:
             result["_quant_rng_state"] = {"version": 2, "seed": self.quant_rng_seed,
                                           "stream": "philox4x32-10"}
@@ -375,6 +426,9 @@ class ZeRO1AdamW4Bit:
                                  "(world, rounds, sizes, recipe) or rank")
             for k, v in self._shard_buffers().items():
                 v.copy_(state_dict["buffers"][k])
+            for st, saved in zip(self.small, state_dict["small"]):
+                for k, v in st.items():
+                    v.copy_(saved[k])
             self.step_count = int(state_dict["step"])
             g = state_dict["param_group"]
             self.lr, self.betas, self.eps, self.wd = g["lr"], tuple(g["betas"]), g["eps"], g["weight_decay"]
@@ -382,16 +436,27 @@ class ZeRO1AdamW4Bit:
         states = state_dict["state"]
         groups = state_dict["param_groups"]
         order = [i for grp in groups for i in grp["params"]]
-        if len(order) != len(self.params):
+        if len(order) != len(self.all_params):
             raise ValueError("state dict holds a different number of parameters")
         masters = state_dict.get("master_weights", {})
         if self.master_weights and not masters:
             raise ValueError("master_weights=True needs FP32 masters in the state dict")
         steps = set()
-        for ti, index in enumerate(order):
+        for i, st_local in zip(self.sindex, self.small):
+            index = order[i]
+            st = states.get(index)
+            if not st or "m1" not in st:
+                raise ValueError(f"parameter {i}: no FP32 moments in the state dict")
+            steps.add(int(st["step"]))
+            st_local["m1"].copy_(st["m1"].reshape(-1))
+            st_local["m2"].copy_(st["m2"].reshape(-1))
+            if "master" in st_local:
+                st_local["master"].copy_(masters[index].reshape(-1).to(torch.float32))
+        for ti, i in enumerate(self.qindex):
+            index = order[i]
             st = states.get(index)
             if not st or "m1_code" not in st:
-                raise ValueError(f"parameter {ti}: no packed 4-bit state in the state dict")
+                raise ValueError(f"parameter {i}: no packed 4-bit state in the state dict")
             steps.add(int(st["step"]))
             for segs in self.segments:
                 for sti, s0, n, so in segs:

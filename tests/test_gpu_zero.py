@@ -13,7 +13,8 @@ import torch.multiprocessing as mp
 
 pytestmark = pytest.mark.gpu
 
-SHAPES = [(4096,), (128, 96), (1024, 64), (8192,), (384, 256)]
+# two tensors below the 4-bit threshold (FP32 moments, replicated on every rank)
+SHAPES = [(4096,), (128, 96), (768,), (1024, 64), (8192,), (100, 3), (384, 256)]
 
 
 def _make(dev, seed=0):
@@ -22,6 +23,24 @@ def _make(dev, seed=0):
     grads = [[(torch.randn(s, generator=g) * 1e-3).to(dev, torch.bfloat16) for s in SHAPES]
              for _ in range(3)]
     return params, grads
+
+
+def _same_state(cons: dict, ref: dict) -> bool:
+    """Bitwise equality of a consolidated ZeRO state and a single-GPU one."""
+    for i, want in ref["state"].items():
+        got = cons["state"][i]
+        for key, val in want.items():
+            if key == "step":
+                if int(got[key]) != int(val):
+                    return False
+            elif key.endswith("_quant_state"):
+                if not torch.equal(got[key]["absmax"].view(torch.int32),
+                                   val["absmax"].cpu().view(torch.int32)):
+                    return False
+            elif not torch.equal(got[key].cpu().reshape(-1).view(torch.uint8),
+                                 val.cpu().reshape(-1).view(torch.uint8)):
+                return False
+    return True
 
 
 def _worker(rank, world, port, recipe, rounds, q, master=False, gather="nccl"):
@@ -70,14 +89,8 @@ def _worker(rank, world, port, recipe, rounds, q, master=False, gather="nccl"):
         # the single-GPU optimizer's codes and scales bit for bit
         cons = opt.state_dict(consolidated=True)
         sref = single.state_dict()
-        for i in sref["state"]:
-            for key in ("m1_code", "m2_code"):
-                if not torch.equal(cons["state"][i][key], sref["state"][i][key].cpu()):
-                    raise AssertionError(f"consolidated {key} of parameter {i} differs")
-            for key in ("m1_quant_state", "m2_quant_state"):
-                if not torch.equal(cons["state"][i][key]["absmax"].view(torch.int32),
-                                   sref["state"][i][key]["absmax"].cpu().view(torch.int32)):
-                    raise AssertionError(f"consolidated {key} of parameter {i} differs")
+        if not _same_state(cons, sref):
+            raise AssertionError("consolidated state differs from the single-GPU state")
         if master:
             # the gathered BF16 model is bf16(the unsharded FP32 params) everywhere,
             # and this rank's FP32 masters equal the unsharded params it owns
@@ -86,7 +99,7 @@ def _worker(rank, world, port, recipe, rounds, q, master=False, gather="nccl"):
                      for a, b in zip(params, ref))
             for segs in opt.plan.segments:
                 for ti, s0, n, so in segs:
-                    want = ref[ti].detach().reshape(-1)[s0:s0 + n]
+                    want = ref[opt.qindex[ti]].detach().reshape(-1)[s0:s0 + n]
                     ok = ok and torch.equal(opt.master[so:so + n].view(torch.int32),
                                             want.view(torch.int32))
         else:
@@ -152,7 +165,7 @@ def test_zero1_master_weights_on_one_gpu_matches_fp32_step():
         assert torch.equal(a.detach().view(torch.int16), b.detach().to(torch.bfloat16).view(torch.int16))
     for segs in opt.plan.segments:
         for ti, s0, n, so in segs:
-            want = fp32[ti].detach().reshape(-1)[s0:s0 + n]
+            want = fp32[opt.qindex[ti]].detach().reshape(-1)[s0:s0 + n]
             assert torch.equal(opt.master[so:so + n].view(torch.int32), want.view(torch.int32))
 
 
@@ -180,12 +193,7 @@ def test_zero1_consolidated_state_dict_resumes_on_the_single_gpu_optimizer():
     _run(sopt, sa, grads[:2])
     sd = zopt.state_dict(consolidated=True)
     ref = sopt.state_dict()
-    for i in ref["state"]:
-        for key in ("m1_code", "m2_code"):
-            assert torch.equal(sd["state"][i][key], ref["state"][i][key].cpu()), (i, key)
-        for key in ("m1_quant_state", "m2_quant_state"):
-            assert torch.equal(sd["state"][i][key]["absmax"].view(torch.int32),
-                               ref["state"][i][key]["absmax"].cpu().view(torch.int32)), (i, key)
+    assert _same_state(sd, ref)
     # ZeRO -> single GPU
     sb = [torch.nn.Parameter(p.detach().clone()) for p in za]
     for p in sb:
