@@ -26,7 +26,7 @@ __global__ void __launch_bounds__(kThreads)
 quantize_kernel(const __grid_constant__ aw4_scheme scheme, int eden, const float* x,
                 int64_t n_blocks, uint8_t* codes, float* scales, const float* draws,
                 uint64_t key, uint32_t step, uint32_t ordinal, float sr_bias, float sr_eps,
-                float one) {
+                float sr_rbias, float one) {
     __shared__ __align__(16) SmemScheme S;
     __shared__ __align__(16) float scratch[kThreads / 32][kWarpScratch];
     load_scheme(S, scheme, threadIdx.x, kThreads);
@@ -64,7 +64,7 @@ quantize_kernel(const __grid_constant__ aw4_scheme scheme, int eden, const float
         if (MODE != AW4_RTN || eden) ok = none_tiny_warp(v, ok);
         const uint32_t c = __all_sync(0xffffffffu, ok)
                                ? encode_fast<MODE>(S, R, g, v, sc, u, scheme.zero_floor, eden,
-                                                   sr_bias, sr_eps, &s)
+                                                   sr_bias, sr_eps, sr_rbias, one, &s)
                                : encode_block<MODE>(S, R, g, v, amax, u, scheme.zero_floor, eden,
                                                     sr_bias, sr_eps, &s);
         if (active) {
@@ -157,21 +157,22 @@ extern "C" int32_t aw4_quantize_blocks(const aw4_scheme* scheme, int32_t eden, c
     const int64_t tiles = (n_blocks + kBlocksPerTile - 1) / kBlocksPerTile;
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(tiles, (int64_t)std::max(sms, 1) * 4));
     cudaStream_t s = (cudaStream_t)stream;
+    const float rbias = sr_fast_rbias(sr_bias, sr_eps);
     switch (scheme->round_mode) {
     case AW4_RTN:
         quantize_kernel<AW4_RTN><<<grid, kThreads, 0, s>>>(*scheme, eden, x, n_blocks, codes, scales,
                                                            draws, key, step, ordinal, sr_bias, sr_eps,
-                                                           1.0f);
+                                                           rbias, 1.0f);
         break;
     case AW4_SR_VALUE:
         quantize_kernel<AW4_SR_VALUE><<<grid, kThreads, 0, s>>>(*scheme, eden, x, n_blocks, codes,
                                                                 scales, draws, key, step, ordinal,
-                                                                sr_bias, sr_eps, 1.0f);
+                                                                sr_bias, sr_eps, rbias, 1.0f);
         break;
     case AW4_SR_UPDATE:
         quantize_kernel<AW4_SR_UPDATE><<<grid, kThreads, 0, s>>>(*scheme, eden, x, n_blocks, codes,
                                                                  scales, draws, key, step, ordinal,
-                                                                 sr_bias, sr_eps, 1.0f);
+                                                                 sr_bias, sr_eps, rbias, 1.0f);
         break;
     default:
         return fail(AW4_ERR_INVALID, "aw4_quantize_blocks: bad round mode");

@@ -146,6 +146,16 @@ __device__ __forceinline__ bool any_tiny(const float v[8]) {
     return m < lim;
 }
 
+// True if some value is a nonzero of magnitude below `lim` (a power of two).
+__device__ __forceinline__ bool any_tiny_below(const float v[8], float lim) {
+    if (lane_absmin(v) >= lim) return false;
+    const uint32_t l = 2u * (uint32_t)__float_as_int(lim) - 1u;
+    uint32_t m = 0xffffffffu;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) m = min(m, 2u * (uint32_t)__float_as_int(v[i]) - 1u);
+    return m < l;
+}
+
 // Branch-free form of any_tiny, for warp votes: the lane minimum decides
 // most lanes; the exact per-value test is evaluated only when some lane of
 // the warp needs it (the vote keeps that branch uniform).

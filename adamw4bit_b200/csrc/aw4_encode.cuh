@@ -29,7 +29,17 @@ constexpr int kEdenDen = 160;                      // denominator table offset
 constexpr int kEdenGroup = 336;                    // second group's offset (16 mod 32)
 constexpr int kEdenTotals = 656;                   // 2 groups x 16 floats
 constexpr int kSrLevels = kEdenTotals + 32;        // 2 groups x 16 floats
-constexpr int kWarpScratch = kSrLevels + 32;       // 720 floats
+constexpr int kSrIntervals = kSrLevels + 32;       // 2 groups x 16 float2
+constexpr int kWarpScratch = kSrIntervals + 64;    // 784 floats
+
+// RN(1 / bias) for the fast update-SR encoder, or 0 (fast encoder off) unless
+// bias lies in [2^-100, 1] and eps in [2^-100, 2^25], the ranges its exactness
+// argument covers.  Host code: the float32 division is correctly rounded.
+inline float sr_fast_rbias(float bias, float eps) {
+    if (!(bias >= 0x1p-100f && bias <= 1.0f && eps >= 0x1p-100f && eps <= 0x1p25f)) return 0.0f;
+    volatile float one = 1.0f;
+    return one / bias;
+}
 static_assert(kEdenGroup % 32 == 16 && kEdenDen % 32 == 0, "bank offsets");
 static_assert(kEdenDen >= kEdenTable && kEdenGroup >= kEdenDen + kEdenTable, "tables overlap");
 static_assert(kEdenTotals >= kEdenGroup + kEdenDen + kEdenTable && kEdenTotals % 4 == 0, "");
@@ -40,6 +50,7 @@ struct GroupCtx {
     const float* rd;   // the column this lane reduces (numerator or denominator table)
     float* totals;     // this group's 16 interleaved column totals
     float* levels;     // 16 floats: update-SR preconditioner of each level
+    float2* sr_int;    // 16 (divisor, its reciprocal) pairs: update-SR intervals
     int j;             // lane within the group (0..15)
     int lane;          // lane within the warp
     float one;         // 1.0 at run time (packed additions)
@@ -54,6 +65,7 @@ __device__ __forceinline__ GroupCtx group_ctx(float* warp_scratch, int lane, flo
     g.rd = (g.j < 8 ? g.tab_num : g.tab_den) + kEdenCol * (g.j & 7);
     g.totals = warp_scratch + kEdenTotals + 16 * h;
     g.levels = warp_scratch + kSrLevels + 16 * h;
+    g.sr_int = reinterpret_cast<float2*>(warp_scratch + kSrIntervals) + 16 * h;
     g.lane = lane;
     g.one = one;
     return g;
@@ -220,9 +232,23 @@ template <int MODE>
 __device__ __forceinline__ uint32_t encode_fast_codes(const SmemScheme& S, const SchemeRegs& R,
                                                       const GroupCtx& g, const float v[8],
                                                       float sc, const float u[8], int zero_floor,
-                                                      int eden, float sr_bias, float sr_eps) {
+                                                      int eden, float sr_bias, float sr_eps,
+                                                      float sr_rbias, float one) {
+    bool int_ok = true;
     if (MODE == AW4_SR_UPDATE) {
-        g.levels[g.j] = precond(sc, S.cb[g.j], sr_bias, sr_eps);
+        // the block's level preconditioners, then per interval k (levels k-1,
+        // k) the quotient's divisor max(f[k-1] - f[k], 1e-30) and its IEEE
+        // reciprocal; a negative reciprocal marks an interval whose p is 1
+        const float fk = precond(sc, S.cb[g.j], sr_bias, sr_eps);
+        g.levels[g.j] = fk;
+        __syncwarp();
+        if (g.j >= 1) {
+            const float den = fsub(g.levels[g.j - 1], fk);
+            const float dl = max_nan(den, 1e-30f);
+            const bool valid = fsub(S.cb[g.j], S.cb[g.j - 1]) > 0.0f && den > 0.0f;
+            g.sr_int[g.j] = make_float2(dl, valid ? frcp(dl) : -1.0f);
+            int_ok = !valid || (dl >= 0x1p-60f && dl <= 0x1p60f);
+        }
         __syncwarp();
     }
     float x[8];
@@ -231,12 +257,65 @@ __device__ __forceinline__ uint32_t encode_fast_codes(const SmemScheme& S, const
     const int floor_code = (MODE != AW4_RTN && zero_floor) ? 1 : 0;
     int idxs[8];
     lut_search8(R, x, idxs);
+    bool sr_done = false;
+    if (MODE == AW4_SR_UPDATE && sr_rbias > 0.0f) {
+        // The preconditioner of each x and the probability quotient by the
+        // correctly rounded fast operations: Markstein against the bias
+        // (sr_rbias = RN(1 / bias)), sqrt_nr, rcp_nr, Markstein against the
+        // interval's divisor.  Preconditions (voted over the warp; otherwise
+        // the IEEE rule below runs): every s*x is 0 or of magnitude >= 2^-100,
+        // so with bias in [2^-100, 1] the quotient s*x/bias is 0 or in
+        // [2^-100, 2^126] (sqrt_nr's exact range) and root + eps in
+        // [2^-100, 2^64] (rcp_nr's); every interval divisor lies in
+        // [2^-60, 2^60] and every numerator fx - f[r] is 0 or of magnitude
+        // >= 2^-60, so the probability quotient is normal and its remainder
+        // exact.  The host checked bias and eps (sr_rbias = 0 otherwise).
+        float t1[8];
+        vmuls8(t1, x, sc);
+        bool ok = int_ok && !any_tiny(t1);
+        if (__all_sync(0xffffffffu, ok)) {
+            float fx[8], pnum[8];
+            const f2 rb = pk2(sr_rbias, sr_rbias), nb = pk2(-sr_bias, -sr_bias);
+            const f2 ee = pk2(sr_eps, sr_eps), oo = pk2(one, one), no = pk2(-one, -one);
+#pragma unroll
+            for (int i = 0; i < 8; i += 2) {
+                const f2 a = pk2(t1[i], t1[i + 1]);
+                const f2 q0 = f2_mul(a, rb);
+                const f2 r0 = f2_fma(q0, nb, a);
+                float t2a, t2b;
+                upk2(f2_fma(r0, rb, q0), t2a, t2b);          // s*x / bias
+                const f2 root = pk2(sqrt_nr(max_nan(t2a, 0.0f)), sqrt_nr(max_nan(t2b, 0.0f)));
+                float da, db;
+                upk2(f2_fma(root, oo, ee), da, db);           // root + eps
+                fx[i] = rcp_nr(da);
+                fx[i + 1] = rcp_nr(db);
+            }
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int r = min(idxs[i], 15);
+                pnum[i] = ffma(g.levels[r], -one, fx[i]);   // fx - f[r]
+            }
+            if (__all_sync(0xffffffffu, !any_tiny_below(pnum, 0x1p-60f))) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int idx = idxs[i];
+                    const int l = max(idx - 1, 0), r = min(idx, 15);
+                    const float2 dv = g.sr_int[min(max(idx, 1), 15)];
+                    float p = div_markstein(pnum[i], dv.x, dv.y);
+                    p = (dv.y < 0.0f) ? 1.0f : p;
+                    p = min_nan(max_nan(p, 0.0f), 1.0f);
+                    code[i] = max((u[i] < p) ? l : r, floor_code);
+                }
+                sr_done = true;
+            }
+        }
+    }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const int idx = idxs[i];
         if (MODE == AW4_RTN) {
             code[i] = idx;  // the dyn4_nz floor is folded into the RTN table
-        } else {
+        } else if (!sr_done) {
             code[i] = (MODE == AW4_SR_VALUE)
                           ? value_sr_from_index(S.cb, idx, x[i], u[i])
                           : update_sr_from_index(S.cb, g.levels, idx, x[i], sc, sr_bias, sr_eps,
@@ -274,8 +353,10 @@ template <int MODE>
 __device__ __forceinline__ uint32_t encode_fast(const SmemScheme& S, const SchemeRegs& R,
                                                 const GroupCtx& g, const float v[8], float sc,
                                                 const float u[8], int zero_floor, int eden,
-                                                float sr_bias, float sr_eps, float* scale_out) {
-    const uint32_t c = encode_fast_codes<MODE>(S, R, g, v, sc, u, zero_floor, eden, sr_bias, sr_eps);
+                                                float sr_bias, float sr_eps, float sr_rbias,
+                                                float one, float* scale_out) {
+    const uint32_t c = encode_fast_codes<MODE>(S, R, g, v, sc, u, zero_floor, eden, sr_bias,
+                                               sr_eps, sr_rbias, one);
     *scale_out = encode_fast_scale(g, sc, eden);
     return c;
 }

@@ -65,6 +65,7 @@ struct KDesc {
 struct HyperDev {
     float w1, w2, decay, neg_step;
     float sqrt_bc2, eps, sr_bias, rcp_sqrt_bc2;   // rcp: RN(1 / sqrt_bc2)
+    float sr_rbias;                               // RN(1 / sr_bias), 0: fast update SR off
     float pos_step;                               // lr / bc1 = -neg_step
     float bsc, rbsc;                              // sqrt_bc2 * 2^24 and RN(1 / bsc)
     float m1_fast_max, m2_fast_max;               // lane bounds of the fast path (-1: off)
@@ -269,10 +270,12 @@ step_kernel(const __grid_constant__ StepLaunch L) {
                 if (M1 != AW4_RTN) load_uniforms(u, D.d1, H.m1_key, H, D, e0, true);
                 float ns1, ns2;
                 const uint32_t c1 =
-                    encode_fast<M1>(sm.s1, r1, g, m1, sc1, u, 0, 0, H.sr_bias, H.eps, &ns1);
+                    encode_fast<M1>(sm.s1, r1, g, m1, sc1, u, 0, 0, H.sr_bias, H.eps, H.sr_rbias,
+                                    one, &ns1);
                 if (M2 != AW4_RTN) load_uniforms(u, D.d2, H.m2_key, H, D, e0, true);
                 const uint32_t c2 =
-                    encode_fast<M2>(sm.s2, r2, g, m2, sc2, u, zf2, L.eden, H.sr_bias, H.eps, &ns2);
+                    encode_fast<M2>(sm.s2, r2, g, m2, sc2, u, zf2, L.eden, H.sr_bias, H.eps,
+                                    H.sr_rbias, one, &ns2);
                 __stcs(reinterpret_cast<unsigned int*>(D.c1 + (e0 >> 1)), c1);
                 __stcs(reinterpret_cast<unsigned int*>(D.c2 + (e0 >> 1)), c2);
                 if (g.j == 0) {
@@ -458,6 +461,7 @@ static HyperDev hyper_dev(const aw4_hyper& h, const aw4_scheme& m2s) {
     d.sqrt_bc2 = h.sqrt_bc2;
     d.eps = h.eps;
     d.sr_bias = h.sr_bias;
+    d.sr_rbias = sr_fast_rbias(h.sr_bias, h.eps);
     d.step = h.step;
     d.m1_key = h.m1_key;
     d.m2_key = h.m2_key;

@@ -287,7 +287,7 @@ def run_reference_torch(args, rank, device: str, eager: bool):
 
 
 def run_ours(args, rank, world, local):
-    from adamw4bit_b200 import ZEEDENAdamW4Bit, _native
+    from adamw4bit_b200 import ZEEDENAdamW4Bit, ZIPSRAdamW4Bit, _native
     from adamw4bit_b200.zero import ZeRO1AdamW4Bit
 
     dev = torch.device("cuda", local)
@@ -302,13 +302,15 @@ def run_ours(args, rank, world, local):
     params, grads = make_workload(dev, shapes,
                                   param_dtype=torch.bfloat16 if master else torch.float32)
     if world == 1:
-        opt = ZEEDENAdamW4Bit(params, lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+        cls = ZEEDENAdamW4Bit if args.recipe == "ze-eden" else ZIPSRAdamW4Bit
+        opt = cls(params, lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1,
+                  quant_rng_seed=None if args.recipe == "ze-eden" else 1234)
         step_fn = opt.step
         updated_per_rank = total
     else:
         # FP32 masters sharded over the ranks; with --gather bf16 the model is
         # BF16 (written by the update kernel) and the all-gather moves 2 B/value
-        opt = ZeRO1AdamW4Bit(params, recipe="ze-eden", rounds=args.rounds,
+        opt = ZeRO1AdamW4Bit(params, recipe=args.recipe, rounds=args.rounds,
                              master_weights=master, reserve_sms=args.reserve_sms,
                              gather="multicast" if args.gather == "multicast" else "nccl")
         step_fn = opt.step
@@ -362,7 +364,8 @@ def run_ours(args, rank, world, local):
                 "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
                 "peak_source": peak_src,
                 "algorithmic_bytes_per_value": b_per_elem,
-                "kernel": "aw4::step_kernel<F32,BF16,RTN,RTN> (fused decode+AdamW+encode)",
+                "kernel": "aw4::step_kernel<F32,BF16,RTN,%s> (fused decode+AdamW+encode)"
+                          % ("RTN" if args.recipe == "ze-eden" else "SR_UPDATE"),
                 "launch_ms": round(per_launch_ms, 4), "values_per_launch": int(per_launch_elems)}
 
     e2e = None
@@ -375,9 +378,11 @@ def run_ours(args, rank, world, local):
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
                 "dtype": "f32", "data": "synthetic",
-                "config": {"workload": WORKLOAD, "values": total, "tensors": len(shapes),
+                "config": {"workload": WORKLOAD if args.recipe == "ze-eden" else
+                           WORKLOAD.replace("ZE-EDEN", "ZIP-SR").replace(" (BASELINE config 5)", ""),
+                           "values": total, "tensors": len(shapes),
                            "param_dtype": "fp32 master + bf16 model copy" if master else "fp32",
-                           "grad_dtype": "bf16", "recipe": "ZE-EDEN",
+                           "grad_dtype": "bf16", "recipe": args.recipe.upper(),
                            "parallelism": "single GPU" if world == 1 else
                            f"zero1-dp{world}, {'bf16 model' if master else 'fp32'} gather "
                            f"({getattr(opt, 'gather_mode', 'nccl')})",
@@ -471,6 +476,8 @@ def main():
                                        "reference-cpu", "reference-cpu-eager"],
                     default="ours")
     ap.add_argument("--rounds", type=int, default=4, help="ZeRO-1 gather rounds")
+    ap.add_argument("--recipe", choices=["ze-eden", "zip-sr"], default="ze-eden",
+                    help="the optimizer recipe (BASELINE config 5 is ZE-EDEN)")
     ap.add_argument("--reserve-sms", type=int, default=16,
                     help="N>1: SMs the update grid leaves to the concurrent all-gather")
     ap.add_argument("--gather", choices=["multicast", "bf16", "fp32"], default="bf16",
