@@ -25,8 +25,8 @@ template <int MODE>
 __global__ void __launch_bounds__(kThreads)
 quantize_kernel(const __grid_constant__ aw4_scheme scheme, int eden, const float* x,
                 int64_t n_blocks, uint8_t* codes, float* scales, const float* draws,
-                uint64_t key, uint32_t step, uint32_t ordinal, float sr_bias, float sr_eps,
-                float sr_rbias, float one) {
+                const PhiloxKey key, uint32_t step, uint32_t ordinal, float sr_bias,
+                float sr_eps, float sr_rbias, float one) {
     __shared__ __align__(16) SmemScheme S;
     __shared__ __align__(16) float scratch[kThreads / 32][kWarpScratch];
     load_scheme(S, scheme, threadIdx.x, kThreads);
@@ -47,10 +47,13 @@ quantize_kernel(const __grid_constant__ aw4_scheme scheme, int eden, const float
             for (int i = 0; i < 8; ++i) v[i] = 0.0f;
         }
         if (MODE != AW4_RTN) {
+            // update SR takes its draws scaled by 2^24 (exact)
+            constexpr bool scaled = MODE == AW4_SR_UPDATE;
             if (draws != nullptr && active) {
                 Elem<AW4_F32>::load8(draws, e0, u);
+                if (scaled) vmuls8(u, u, 0x1p24f);
             } else {
-                philox_uniform8(key, step, ordinal, (uint64_t)e0, u);
+                philox_uniform8<scaled>(key, step, ordinal, (uint64_t)e0, u);
             }
         }
         // the step kernel's dispatch: one warp vote selects the branch-free
@@ -62,6 +65,8 @@ quantize_kernel(const __grid_constant__ aw4_scheme scheme, int eden, const float
         const float sc = max_nan(gmax, kScaleFloor);
         bool ok = sc <= kMarksteinMaxDivisor && (gmax >= kScaleFloor || !eden);   // false for NaN / inf
         if (MODE != AW4_RTN || eden) ok = none_tiny_warp(v, ok);
+        // the fast update-SR encoder takes non-negative values (moments m2)
+        if (MODE == AW4_SR_UPDATE) ok = ok && lane_min(v) >= 0.0f;
         const uint32_t c = __all_sync(0xffffffffu, ok)
                                ? encode_fast<MODE>(S, R, g, v, sc, u, scheme.zero_floor, eden,
                                                    sr_bias, sr_eps, sr_rbias, one, &s)
@@ -158,20 +163,21 @@ extern "C" int32_t aw4_quantize_blocks(const aw4_scheme* scheme, int32_t eden, c
     const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(tiles, (int64_t)std::max(sms, 1) * 4));
     cudaStream_t s = (cudaStream_t)stream;
     const float rbias = sr_fast_rbias(sr_bias, sr_eps);
+    const PhiloxKey pk = philox_schedule(key);
     switch (scheme->round_mode) {
     case AW4_RTN:
         quantize_kernel<AW4_RTN><<<grid, kThreads, 0, s>>>(*scheme, eden, x, n_blocks, codes, scales,
-                                                           draws, key, step, ordinal, sr_bias, sr_eps,
+                                                           draws, pk, step, ordinal, sr_bias, sr_eps,
                                                            rbias, 1.0f);
         break;
     case AW4_SR_VALUE:
         quantize_kernel<AW4_SR_VALUE><<<grid, kThreads, 0, s>>>(*scheme, eden, x, n_blocks, codes,
-                                                                scales, draws, key, step, ordinal,
+                                                                scales, draws, pk, step, ordinal,
                                                                 sr_bias, sr_eps, rbias, 1.0f);
         break;
     case AW4_SR_UPDATE:
         quantize_kernel<AW4_SR_UPDATE><<<grid, kThreads, 0, s>>>(*scheme, eden, x, n_blocks, codes,
-                                                                 scales, draws, key, step, ordinal,
+                                                                 scales, draws, pk, step, ordinal,
                                                                  sr_bias, sr_eps, rbias, 1.0f);
         break;
     default:

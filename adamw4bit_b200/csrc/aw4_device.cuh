@@ -132,6 +132,14 @@ __device__ __forceinline__ float lane_absmin(const float v[8]) {
     return fminf(a, fabsf(v[7]));
 }
 
+// Min of a lane's 8 values (a NaN operand is ignored).
+__device__ __forceinline__ float lane_min(const float v[8]) {
+    float a = min3(v[0], v[1], v[2]);
+    a = min3(a, v[3], v[4]);
+    a = min3(a, v[5], v[6]);
+    return fminf(a, v[7]);
+}
+
 // True if some value is a nonzero of magnitude below 2^-100 (such a lane
 // takes the IEEE division path instead of div_markstein).  A lane whose
 // smallest magnitude is at least 2^-100 is decided by one compare; otherwise
@@ -144,16 +152,6 @@ __device__ __forceinline__ bool any_tiny(const float v[8]) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) m = min(m, 2u * (uint32_t)__float_as_int(v[i]) - 1u);
     return m < lim;
-}
-
-// True if some value is a nonzero of magnitude below `lim` (a power of two).
-__device__ __forceinline__ bool any_tiny_below(const float v[8], float lim) {
-    if (lane_absmin(v) >= lim) return false;
-    const uint32_t l = 2u * (uint32_t)__float_as_int(lim) - 1u;
-    uint32_t m = 0xffffffffu;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) m = min(m, 2u * (uint32_t)__float_as_int(v[i]) - 1u);
-    return m < l;
 }
 
 // Branch-free form of any_tiny, for warp votes: the lane minimum decides
@@ -351,30 +349,52 @@ struct Elem<AW4_F16> {
 // (e/4 low word, e/4 high word, step, ordinal); key = 64-bit stream key;
 // element e takes word e%4, top 24 bits -> uniform in [0, 1).
 // ---------------------------------------------------------------------------
-__device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint32_t k0, uint32_t k1) {
-#pragma unroll
+// The key schedule: round r uses (k0 + r*0x9E3779B9, k1 + r*0xBB67AE85).  The
+// host computes it once per launch, so each round XORs kernel-parameter
+// operands instead of advancing the key.
+struct PhiloxKey {
+    uint32_t k[20];   // (k0, k1) of rounds 0..9
+};
+inline PhiloxKey philox_schedule(uint64_t key) {
+    PhiloxKey s;
+    uint32_t k0 = (uint32_t)key, k1 = (uint32_t)(key >> 32);
     for (int r = 0; r < 10; ++r) {
-        const uint32_t hi0 = __umulhi(0xD2511F53u, c.x), lo0 = 0xD2511F53u * c.x;
-        const uint32_t hi1 = __umulhi(0xCD9E8D57u, c.z), lo1 = 0xCD9E8D57u * c.z;
-        c = make_uint4(hi1 ^ c.y ^ k0, lo1, hi0 ^ c.w ^ k1, lo0);
+        s.k[2 * r] = k0;
+        s.k[2 * r + 1] = k1;
         k0 += 0x9E3779B9u;
         k1 += 0xBB67AE85u;
+    }
+    return s;
+}
+
+__device__ __forceinline__ uint4 philox4x32_10(uint4 c, const PhiloxKey& K) {
+#pragma unroll
+    for (int r = 0; r < 10; ++r) {
+        const uint64_t p0 = (uint64_t)0xD2511F53u * c.x;   // one widening multiply each
+        const uint64_t p1 = (uint64_t)0xCD9E8D57u * c.z;
+        c = make_uint4((uint32_t)(p1 >> 32) ^ c.y ^ K.k[2 * r], (uint32_t)p1,
+                       (uint32_t)(p0 >> 32) ^ c.w ^ K.k[2 * r + 1], (uint32_t)p0);
     }
     return c;
 }
 
 __device__ __forceinline__ float u24(uint32_t r) { return (float)(r >> 8) * 0x1p-24f; }
+// The same draw scaled by 2^24: the integer r >> 8 as a float (exact).
+__device__ __forceinline__ float k24(uint32_t r) { return (float)(r >> 8); }
 
-// 8 uniforms for elements e .. e+7 (e a multiple of 4) of one stream.
-__device__ __forceinline__ void philox_uniform8(uint64_t key, uint32_t step, uint32_t ordinal,
-                                                uint64_t e, float u[8]) {
+// 8 uniforms for elements e .. e+7 (e a multiple of 4) of one stream; with
+// SCALED, the uniforms times 2^24 (the preconditioner-space SR rule compares
+// them with a probability scaled the same way).
+template <bool SCALED = false>
+__device__ __forceinline__ void philox_uniform8(const PhiloxKey& K, uint32_t step,
+                                                uint32_t ordinal, uint64_t e, float u[8]) {
     const uint64_t q = e >> 2;
-    const uint32_t k0 = (uint32_t)key, k1 = (uint32_t)(key >> 32);
-    uint4 r0 = philox4x32_10(make_uint4((uint32_t)q, (uint32_t)(q >> 32), step, ordinal), k0, k1);
+    uint4 r0 = philox4x32_10(make_uint4((uint32_t)q, (uint32_t)(q >> 32), step, ordinal), K);
     uint4 r1 = philox4x32_10(
-        make_uint4((uint32_t)(q + 1), (uint32_t)((q + 1) >> 32), step, ordinal), k0, k1);
-    u[0] = u24(r0.x); u[1] = u24(r0.y); u[2] = u24(r0.z); u[3] = u24(r0.w);
-    u[4] = u24(r1.x); u[5] = u24(r1.y); u[6] = u24(r1.z); u[7] = u24(r1.w);
+        make_uint4((uint32_t)(q + 1), (uint32_t)((q + 1) >> 32), step, ordinal), K);
+    const uint32_t w[8] = {r0.x, r0.y, r0.z, r0.w, r1.x, r1.y, r1.z, r1.w};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) u[i] = SCALED ? k24(w[i]) : u24(w[i]);
 }
 
 // ---------------------------------------------------------------------------
@@ -456,26 +476,30 @@ __device__ __forceinline__ int lut_search(const SmemScheme& s, const SchemeRegs&
     return count - ge;
 }
 
-// lut_search over a lane's 8 values, the bin indices computed pairwise by
-// packed round-toward-zero FMAs.
-__device__ __forceinline__ void lut_search8(const SchemeRegs& r, const float x[8], int code[8]) {
-    const f2 hh = pk2(r.half, r.half), bb = pk2(r.bias, r.bias);
+// lut_search of a pair of values, the bin indices computed by one packed
+// round-toward-zero FMA.
+__device__ __forceinline__ void lut_search2(const SchemeRegs& r, float x0, float x1, int code[2]) {
+    f2 t;
+    asm("fma.rz.f32x2 %0, %1, %2, %3;"
+        : "=l"(t)
+        : "l"(pk2(x0, x1)), "l"(pk2(r.half, r.half)), "l"(pk2(r.bias, r.bias)));
+    float b0, b1;
+    upk2(t, b0, b1);
 #pragma unroll
-    for (int i = 0; i < 8; i += 2) {
-        f2 t;
-        asm("fma.rz.f32x2 %0, %1, %2, %3;" : "=l"(t) : "l"(pk2(x[i], x[i + 1])), "l"(hh), "l"(bb));
-        float b0, b1;
-        upk2(t, b0, b1);
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-            const uint32_t addr = __float_as_uint(k ? b1 : b0) * 8u + r.tab_biased;
-            float next;
-            int count, ge;
-            asm("ld.shared.v2.b32 {%0, %1}, [%2];" : "=f"(next), "=r"(count) : "r"(addr));
-            asm("set.ge.s32.f32 %0, %1, %2;" : "=r"(ge) : "f"(x[i + k]), "f"(next));
-            code[i + k] = count - ge;
-        }
+    for (int k = 0; k < 2; ++k) {
+        const uint32_t addr = __float_as_uint(k ? b1 : b0) * 8u + r.tab_biased;
+        float next;
+        int count, ge;
+        asm("ld.shared.v2.b32 {%0, %1}, [%2];" : "=f"(next), "=r"(count) : "r"(addr));
+        asm("set.ge.s32.f32 %0, %1, %2;" : "=r"(ge) : "f"(k ? x1 : x0), "f"(next));
+        code[k] = count - ge;
     }
+}
+
+// lut_search over a lane's 8 values.
+__device__ __forceinline__ void lut_search8(const SchemeRegs& r, const float x[8], int code[8]) {
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) lut_search2(r, x[i], x[i + 1], code + i);
 }
 
 // Level of a code from the codebook held in registers: lane l keeps

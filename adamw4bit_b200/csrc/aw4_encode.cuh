@@ -29,14 +29,16 @@ constexpr int kEdenDen = 160;                      // denominator table offset
 constexpr int kEdenGroup = 336;                    // second group's offset (16 mod 32)
 constexpr int kEdenTotals = 656;                   // 2 groups x 16 floats
 constexpr int kSrLevels = kEdenTotals + 32;        // 2 groups x 16 floats
-constexpr int kSrIntervals = kSrLevels + 32;       // 2 groups x 16 float2
-constexpr int kWarpScratch = kSrIntervals + 64;    // 784 floats
+constexpr int kSrTable = kSrLevels + 32;           // 2 groups x 17 float4
+constexpr int kWarpScratch = kSrTable + 136;       // 856 floats
+static_assert(kSrTable % 4 == 0, "float4 table");
 
 // RN(1 / bias) for the fast update-SR encoder, or 0 (fast encoder off) unless
-// bias lies in [2^-100, 1] and eps in [2^-100, 2^25], the ranges its exactness
-// argument covers.  Host code: the float32 division is correctly rounded.
+// bias lies in [2^-40, 1] and eps in [2^-60, 2^25], the ranges its exactness
+// argument covers (codebooks lie in [-1, 1], checked by aw4_scheme_prepare).
+// Host code: the float32 division is correctly rounded.
 inline float sr_fast_rbias(float bias, float eps) {
-    if (!(bias >= 0x1p-100f && bias <= 1.0f && eps >= 0x1p-100f && eps <= 0x1p25f)) return 0.0f;
+    if (!(bias >= 0x1p-40f && bias <= 1.0f && eps >= 0x1p-60f && eps <= 0x1p25f)) return 0.0f;
     volatile float one = 1.0f;
     return one / bias;
 }
@@ -50,7 +52,7 @@ struct GroupCtx {
     const float* rd;   // the column this lane reduces (numerator or denominator table)
     float* totals;     // this group's 16 interleaved column totals
     float* levels;     // 16 floats: update-SR preconditioner of each level
-    float2* sr_int;    // 16 (divisor, its reciprocal) pairs: update-SR intervals
+    float4* sr_tab;    // 17 entries: the fast update-SR rule's interval table
     int j;             // lane within the group (0..15)
     int lane;          // lane within the warp
     float one;         // 1.0 at run time (packed additions)
@@ -65,7 +67,7 @@ __device__ __forceinline__ GroupCtx group_ctx(float* warp_scratch, int lane, flo
     g.rd = (g.j < 8 ? g.tab_num : g.tab_den) + kEdenCol * (g.j & 7);
     g.totals = warp_scratch + kEdenTotals + 16 * h;
     g.levels = warp_scratch + kSrLevels + 16 * h;
-    g.sr_int = reinterpret_cast<float2*>(warp_scratch + kSrIntervals) + 16 * h;
+    g.sr_tab = reinterpret_cast<float4*>(warp_scratch + kSrTable) + 17 * h;
     g.lane = lane;
     g.one = one;
     return g;
@@ -131,6 +133,56 @@ __device__ __forceinline__ float2 eden_sums(const GroupCtx& g, const float np[8]
     return eden_finish(g);
 }
 
+// 2^24 precond(s, level): the fast exact sequence (Markstein by the bias,
+// sqrt_nr, rcp_nr of the scaled sum) when s*level is 0 or at least 2^-100
+// (so s*level/bias is 0 or in sqrt_nr's exact range), else the IEEE
+// operations.  Scaling the last sum by 2^-24 is exact (it stays normal), so
+// the reciprocal is 2^24 RN(1/(root + eps)).
+__device__ __forceinline__ float precond24(float s, float level, float bias, float rbias,
+                                           float eps) {
+    const float t = fmul(s, level);
+    if (t == 0.0f || t >= kMarksteinMinNumerator) {
+        const float root = sqrt_nr(div_markstein(t, bias, rbias));
+        return rcp_nr(ffma(root, 0x1p-24f, fmul(eps, 0x1p-24f)));
+    }
+    return fmul(precond(s, level, bias, eps), 0x1p24f);
+}
+
+// The fast update-SR rule's per-block table (quantization.py:336-377 with the
+// reference's f[k] = precond(s, cb[k])).  Entry i, for the searchsorted-left
+// index i of a value (l = max(i-1, 0), r = min(i, 15)):
+//   x: 2^24 f[r]
+//   y: the quotient's divisor f[l] - f[r]
+//   z: RN(1 / divisor), or 0 where the code does not depend on the draw
+//   w: the code taken when the draw is not below p (int bits)
+// With the zero floor applied to both codes, entries whose two codes
+// coincide, and intervals for which the reference sets p = 1 (no positive
+// width or divisor: the code is l for every draw in [0, 1)), have z = 0, so
+// the Markstein quotient is zero and code w is taken.  Preconditions (host
+// and caller): bias in [2^-40, 1], eps in [2^-60, 2^25], s <= 2^26 and
+// |cb| <= 1.  Then every f lies in [2^-34, 2^60], so a positive divisor lies
+// in [2^-57, 2^60], inside rcp_nr's exact range.
+__device__ __forceinline__ void sr_table(const GroupCtx& g, const SmemScheme& S, float sc,
+                                         int floor_code, float bias, float rbias, float eps) {
+    const int j = g.j;
+    const float fj = precond24(sc, S.cb[j], bias, rbias, eps);
+    const float fprev = __shfl_up_sync(0xffffffffu, fj, 1, 16);
+    float dl = 1.0f, y = 0.0f;
+    int rc = max(j, floor_code);
+    if (j >= 1) {
+        const int lc = max(j - 1, floor_code);
+        const float den = fsub(fprev, fj);   // 2^24 (f[l] - f[r]), exactly
+        if (fsub(S.cb[j], S.cb[j - 1]) > 0.0f && den > 0.0f) {
+            dl = fmul(den, 0x1p-24f);
+            if (lc != rc) y = rcp_nr(dl);
+        } else {
+            rc = lc;
+        }
+    }
+    g.sr_tab[j] = make_float4(fj, dl, y, __int_as_float(rc));
+    if (j == 15) g.sr_tab[16] = make_float4(fj, 1.0f, 0.0f, __int_as_float(15));
+}
+
 // Encodes the group's block.  v: this lane's 8 working values; amax: their
 // lane_absmax.  u: 8 uniforms (SR modes).  Returns this lane's 8 codes packed
 // as nibbles (value 8j+i in bits 4i..4i+3, i.e. the reference's little-endian
@@ -172,7 +224,7 @@ __device__ __forceinline__ uint32_t encode_block(const SmemScheme& S, const Sche
                 code[i] = (MODE == AW4_SR_VALUE)
                               ? value_sr_from_index(S.cb, idx, x[i], u[i])
                               : update_sr_from_index(S.cb, g.levels, idx, x[i], sc, sr_bias,
-                                                     sr_eps, u[i]);
+                                                     sr_eps, fmul(u[i], 0x1p-24f));
                 if (zero_floor) code[i] = max(code[i], 1);
             }
         }
@@ -188,7 +240,7 @@ __device__ __forceinline__ uint32_t encode_block(const SmemScheme& S, const Sche
                 code[i] = (MODE == AW4_SR_VALUE)
                               ? value_sr_from_index(S.cb, idx, x[i], u[i])
                               : update_sr_from_index(S.cb, g.levels, idx, x[i], sc, sr_bias,
-                                                     sr_eps, u[i]);
+                                                     sr_eps, fmul(u[i], 0x1p-24f));
             }
             if (zero_floor) code[i] = max(code[i], 1);
         }
@@ -221,6 +273,69 @@ __device__ __forceinline__ uint32_t encode_block(const SmemScheme& S, const Sche
     return packed;
 }
 
+// The fast update-SR rule over a lane's 8 values, pair by pair: x = v/s by
+// Markstein, the searchsorted index, 2^24 fx by the fast sequence of
+// precond24 (packed where no operand needs a sign change), the table entry of
+// the index, the quotient p' = 2^24 (fx - f[r]) / (f[l] - f[r]) by Markstein,
+// and code = w - (u' < p') with u' = 2^24 u.  Ranges, beyond the table's: v
+// is non-negative (an m2 moment, or the codec's vote) and 0 or >= 2^-100, so
+// s*x is 0 or >= 2^-101, s*x/bias is 0 or in [2^-101, 2^66] and exact by
+// Markstein, and root + eps lies in [2^-60, 2^34]; 2^24 fx and 2^24 f[r] lie
+// in [2^-10, 2^84], so a nonzero difference is at least 2^-33, and the
+// quotient, in [0, 2^24] because precond is non-increasing and x lies in
+// [cb[l], cb[r]], is normal with an exact remainder.  The reference's clamp
+// of p to [0, 1] is then the identity.  Returns the packed codes.
+__device__ __forceinline__ uint32_t encode_fast_upd_sr(const SchemeRegs& R, const GroupCtx& g,
+                                                       const float v[8], float sc,
+                                                       const float u[8], float bias,
+                                                       float rbias, float eps) {
+    const float ys = rcp_nr(sc);
+    const f2 nsc = pk2(-sc, -sc), yss = pk2(ys, ys), scp = pk2(sc, sc);
+    const f2 rb = pk2(rbias, rbias), nb = pk2(-bias, -bias);
+    const f2 hh = pk2(0.5f, 0.5f), s24 = pk2(0x1p-24f, 0x1p-24f);
+    const float eps24 = fmul(eps, 0x1p-24f);
+    const f2 ee = pk2(eps24, eps24);
+    uint32_t packed = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+        // x = v / s (Markstein)
+        const f2 vv = pk2(v[i], v[i + 1]);
+        const f2 xq = f2_mul(vv, yss);
+        const f2 xx = f2_fma(f2_fma(xq, nsc, vv), yss, xq);
+        float x0, x1;
+        upk2(xx, x0, x1);
+        int idx[2];
+        lut_search2(R, x0, x1, idx);
+        // s*x / bias (Markstein)
+        const f2 t1 = f2_mul(xx, scp);
+        const f2 q0 = f2_mul(t1, rb);
+        const f2 t2 = f2_fma(f2_fma(q0, nb, t1), rb, q0);
+        float ta, tb;
+        upk2(t2, ta, tb);
+        // sqrt_nr of both
+        const f2 y = pk2(rsqrt_approx(fmaxf(ta, kNrMin)), rsqrt_approx(fmaxf(tb, kNrMin)));
+        const f2 sq = f2_mul(t2, y), h = f2_mul(hh, y);
+        float sa, sb;
+        upk2(sq, sa, sb);
+        const f2 root = f2_fma(pk2(ffma(-sa, sa, ta), ffma(-sb, sb, tb)), h, sq);
+        // rcp_nr of 2^-24 (root + eps), both
+        float da, db;
+        upk2(f2_fma(root, s24, ee), da, db);
+        const float ra = rcp_approx(da), rbb = rcp_approx(db);
+        const f2 yy = pk2(ra, rbb);
+        float fa, fb;
+        upk2(f2_fma(pk2(ffma(-da, ra, 1.0f), ffma(-db, rbb, 1.0f)), yy, yy), fa, fb);
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const float4 t = g.sr_tab[idx[k]];
+            const float pq = div_markstein(fsub(k ? fb : fa, t.x), t.y, t.z);
+            const int code = __float_as_int(t.w) - (u[i + k] < pq ? 1 : 0);
+            packed += (uint32_t)code << (4 * (i + k));   // disjoint nibbles
+        }
+    }
+    return packed;
+}
+
 // encode_block for a warp whose blocks all meet the fast preconditions (the
 // caller has voted): a finite scale sc = max(absmax, 1e-12) <= 2^26; for SR
 // or EDEN, no nonzero value below 2^-100; for EDEN, absmax >= 1e-12.  The same results as
@@ -234,92 +349,33 @@ __device__ __forceinline__ uint32_t encode_fast_codes(const SmemScheme& S, const
                                                       float sc, const float u[8], int zero_floor,
                                                       int eden, float sr_bias, float sr_eps,
                                                       float sr_rbias, float one) {
-    bool int_ok = true;
-    if (MODE == AW4_SR_UPDATE) {
-        // the block's level preconditioners, then per interval k (levels k-1,
-        // k) the quotient's divisor max(f[k-1] - f[k], 1e-30) and its IEEE
-        // reciprocal; a negative reciprocal marks an interval whose p is 1
-        const float fk = precond(sc, S.cb[g.j], sr_bias, sr_eps);
-        g.levels[g.j] = fk;
+    const int floor_code = (MODE != AW4_RTN && zero_floor) ? 1 : 0;
+    if (MODE == AW4_SR_UPDATE && sr_rbias > 0.0f && !eden) {   // launch-uniform
+        sr_table(g, S, sc, floor_code, sr_bias, sr_rbias, sr_eps);
         __syncwarp();
-        if (g.j >= 1) {
-            const float den = fsub(g.levels[g.j - 1], fk);
-            const float dl = max_nan(den, 1e-30f);
-            const bool valid = fsub(S.cb[g.j], S.cb[g.j - 1]) > 0.0f && den > 0.0f;
-            g.sr_int[g.j] = make_float2(dl, valid ? frcp(dl) : -1.0f);
-            int_ok = !valid || (dl >= 0x1p-60f && dl <= 0x1p60f);
-        }
+        const uint32_t packed = encode_fast_upd_sr(R, g, v, sc, u, sr_bias, sr_rbias, sr_eps);
+        __syncwarp();   // the table is rebuilt for the next block
+        return packed;
+    }
+    if (MODE == AW4_SR_UPDATE) {
+        g.levels[g.j] = precond(sc, S.cb[g.j], sr_bias, sr_eps);
         __syncwarp();
     }
     float x[8];
     int code[8];
     vdiv_markstein8(x, v, sc, rcp_nr(sc));
-    const int floor_code = (MODE != AW4_RTN && zero_floor) ? 1 : 0;
     int idxs[8];
     lut_search8(R, x, idxs);
-    bool sr_done = false;
-    if (MODE == AW4_SR_UPDATE && sr_rbias > 0.0f) {
-        // The preconditioner of each x and the probability quotient by the
-        // correctly rounded fast operations: Markstein against the bias
-        // (sr_rbias = RN(1 / bias)), sqrt_nr, rcp_nr, Markstein against the
-        // interval's divisor.  Preconditions (voted over the warp; otherwise
-        // the IEEE rule below runs): every s*x is 0 or of magnitude >= 2^-100,
-        // so with bias in [2^-100, 1] the quotient s*x/bias is 0 or in
-        // [2^-100, 2^126] (sqrt_nr's exact range) and root + eps in
-        // [2^-100, 2^64] (rcp_nr's); every interval divisor lies in
-        // [2^-60, 2^60] and every numerator fx - f[r] is 0 or of magnitude
-        // >= 2^-60, so the probability quotient is normal and its remainder
-        // exact.  The host checked bias and eps (sr_rbias = 0 otherwise).
-        float t1[8];
-        vmuls8(t1, x, sc);
-        bool ok = int_ok && !any_tiny(t1);
-        if (__all_sync(0xffffffffu, ok)) {
-            float fx[8], pnum[8];
-            const f2 rb = pk2(sr_rbias, sr_rbias), nb = pk2(-sr_bias, -sr_bias);
-            const f2 ee = pk2(sr_eps, sr_eps), oo = pk2(one, one), no = pk2(-one, -one);
-#pragma unroll
-            for (int i = 0; i < 8; i += 2) {
-                const f2 a = pk2(t1[i], t1[i + 1]);
-                const f2 q0 = f2_mul(a, rb);
-                const f2 r0 = f2_fma(q0, nb, a);
-                float t2a, t2b;
-                upk2(f2_fma(r0, rb, q0), t2a, t2b);          // s*x / bias
-                const f2 root = pk2(sqrt_nr(max_nan(t2a, 0.0f)), sqrt_nr(max_nan(t2b, 0.0f)));
-                float da, db;
-                upk2(f2_fma(root, oo, ee), da, db);           // root + eps
-                fx[i] = rcp_nr(da);
-                fx[i + 1] = rcp_nr(db);
-            }
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int r = min(idxs[i], 15);
-                pnum[i] = ffma(g.levels[r], -one, fx[i]);   // fx - f[r]
-            }
-            if (__all_sync(0xffffffffu, !any_tiny_below(pnum, 0x1p-60f))) {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) {
-                    const int idx = idxs[i];
-                    const int l = max(idx - 1, 0), r = min(idx, 15);
-                    const float2 dv = g.sr_int[min(max(idx, 1), 15)];
-                    float p = div_markstein(pnum[i], dv.x, dv.y);
-                    p = (dv.y < 0.0f) ? 1.0f : p;
-                    p = min_nan(max_nan(p, 0.0f), 1.0f);
-                    code[i] = max((u[i] < p) ? l : r, floor_code);
-                }
-                sr_done = true;
-            }
-        }
-    }
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
         const int idx = idxs[i];
         if (MODE == AW4_RTN) {
             code[i] = idx;  // the dyn4_nz floor is folded into the RTN table
-        } else if (!sr_done) {
+        } else {
             code[i] = (MODE == AW4_SR_VALUE)
                           ? value_sr_from_index(S.cb, idx, x[i], u[i])
                           : update_sr_from_index(S.cb, g.levels, idx, x[i], sc, sr_bias, sr_eps,
-                                                 u[i]);
+                                                 fmul(u[i], 0x1p-24f));
             code[i] = max(code[i], floor_code);
         }
     }

@@ -70,7 +70,7 @@ struct HyperDev {
     float bsc, rbsc;                              // sqrt_bc2 * 2^24 and RN(1 / bsc)
     float m1_fast_max, m2_fast_max;               // lane bounds of the fast path (-1: off)
     uint32_t step;
-    uint64_t m1_key, m2_key;
+    PhiloxKey m1_key, m2_key;                     // key schedules of the SR streams
 };
 
 // One launch covers tensors of one hyper-parameter set, so every scalar is
@@ -176,14 +176,18 @@ __device__ __forceinline__ void store_model_copy(const KDesc& D, int64_t e0, con
 }
 
 // SR uniforms of 8 values: the test-hook draws buffer when given, else the
-// in-kernel Philox stream of the moment.
-__device__ __forceinline__ void load_uniforms(float u[8], const float* draws, uint64_t key,
-                                              const HyperDev& H, const KDesc& D, int64_t e0,
-                                              bool active) {
+// in-kernel Philox stream of the moment.  For the update-SR rule (MODE
+// AW4_SR_UPDATE) they are scaled by 2^24 (exact), the form its encoder takes.
+template <int MODE>
+__device__ __forceinline__ void load_uniforms(float u[8], const float* draws,
+                                              const PhiloxKey& key, const HyperDev& H,
+                                              const KDesc& D, int64_t e0, bool active) {
+    constexpr bool scaled = MODE == AW4_SR_UPDATE;
     if (draws != nullptr && active) {
         Elem<AW4_F32>::load8(draws, e0, u);
+        if (scaled) vmuls8(u, u, 0x1p24f);
     } else {
-        philox_uniform8(key, H.step, D.ordinal, (uint64_t)(D.elem_offset + e0), u);
+        philox_uniform8<scaled>(key, H.step, D.ordinal, (uint64_t)(D.elem_offset + e0), u);
     }
 }
 
@@ -267,12 +271,12 @@ step_kernel(const __grid_constant__ StepLaunch L) {
                 vadd8(p, q, p, one);                 // p.addcdiv_(m1, den, -lr/bc1)
                 Elem<PT>::store8(D.param, e0, p);
                 if (D.pc != nullptr) store_model_copy(D, e0, p);
-                if (M1 != AW4_RTN) load_uniforms(u, D.d1, H.m1_key, H, D, e0, true);
+                if (M1 != AW4_RTN) load_uniforms<M1>(u, D.d1, H.m1_key, H, D, e0, true);
                 float ns1, ns2;
                 const uint32_t c1 =
                     encode_fast<M1>(sm.s1, r1, g, m1, sc1, u, 0, 0, H.sr_bias, H.eps, H.sr_rbias,
                                     one, &ns1);
-                if (M2 != AW4_RTN) load_uniforms(u, D.d2, H.m2_key, H, D, e0, true);
+                if (M2 != AW4_RTN) load_uniforms<M2>(u, D.d2, H.m2_key, H, D, e0, true);
                 const uint32_t c2 =
                     encode_fast<M2>(sm.s2, r2, g, m2, sc2, u, zf2, L.eden, H.sr_bias, H.eps,
                                     H.sr_rbias, one, &ns2);
@@ -301,13 +305,13 @@ step_kernel(const __grid_constant__ StepLaunch L) {
             }
 
             // re-encode m1 (adamw.py:764-771)
-            if (M1 != AW4_RTN) load_uniforms(u, D.d1, H.m1_key, H, D, e0, active);
+            if (M1 != AW4_RTN) load_uniforms<M1>(u, D.d1, H.m1_key, H, D, e0, active);
             float ns1;
             const uint32_t c1 =
                 encode_block<M1>(sm.s1, r1, g, m1, amax1, u, 0, 0, H.sr_bias, H.eps, &ns1);
 
             // re-encode m2 (adamw.py:675-683 update-SR, 795-803 RTN + floor + EDEN)
-            if (M2 != AW4_RTN) load_uniforms(u, D.d2, H.m2_key, H, D, e0, active);
+            if (M2 != AW4_RTN) load_uniforms<M2>(u, D.d2, H.m2_key, H, D, e0, active);
             float ns2;
             const uint32_t c2 =
                 encode_block<M2>(sm.s2, r2, g, m2, amax2, u, zf2, L.eden, H.sr_bias, H.eps, &ns2);
@@ -463,8 +467,8 @@ static HyperDev hyper_dev(const aw4_hyper& h, const aw4_scheme& m2s) {
     d.sr_bias = h.sr_bias;
     d.sr_rbias = sr_fast_rbias(h.sr_bias, h.eps);
     d.step = h.step;
-    d.m1_key = h.m1_key;
-    d.m2_key = h.m2_key;
+    d.m1_key = philox_schedule(h.m1_key);
+    d.m2_key = philox_schedule(h.m2_key);
     d.pos_step = -h.neg_step;
     d.bsc = h.sqrt_bc2 * 0x1p24f;
     // float32 divisions on the host (SSE): correctly rounded

@@ -97,7 +97,7 @@ typedef struct aw4_qtensor {
     float* m1_scales;              /* numel/128 block scales */
     uint8_t* m2_codes;
     float* m2_scales;
-    const float* m1_draws;         /* NULL: Philox; else numel uniforms (test hook) */
+    const float* m1_draws;         /* NULL: Philox; else numel uniforms in [0, 1) (test hook) */
     const float* m2_draws;
     int64_t numel;                 /* multiple of 128 */
     int64_t elem_offset;           /* index of element 0 in the whole tensor (Philox) */
@@ -157,7 +157,8 @@ int32_t aw4_init_zero_state(const aw4_scheme* scheme, int32_t eden, uint8_t* cod
                             float* scales, int64_t numel, int32_t device, void* stream);
 
 /* Standalone block codec (block 128): x[numel] float32 -> packed codes +
- * scales.  draws: NULL for Philox(key, step, ordinal) uniforms.  bias/eps
+ * scales.  draws: NULL for Philox(key, step, ordinal) uniforms, else numel
+ * uniforms in [0, 1).  bias/eps
  * are the update-SR bias correction (clamped at 1e-12) and Adam epsilon. */
 int32_t aw4_quantize_blocks(const aw4_scheme* scheme, int32_t eden, const float* x,
                             int64_t numel, uint8_t* codes, float* scales,
