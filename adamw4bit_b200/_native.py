@@ -21,7 +21,7 @@ F32, BF16, F16 = 0, 1, 2
 RTN, SR_VALUE, SR_UPDATE = 0, 1, 2
 BLOCK = 128
 LUT_BINS = 1024
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 DTYPE_CODES = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}
 
@@ -47,6 +47,7 @@ class Hyper(ctypes.Structure):
         ("neg_step", ctypes.c_float), ("sqrt_bc2", ctypes.c_float), ("eps", ctypes.c_float),
         ("sr_bias", ctypes.c_float), ("step", ctypes.c_uint32),
         ("m1_key", ctypes.c_uint64), ("m2_key", ctypes.c_uint64),
+        ("grad_scale", ctypes.c_float), ("pad", ctypes.c_int32),
     ]
 
 
@@ -59,7 +60,7 @@ class QTensor(ctypes.Structure):
         ("numel", ctypes.c_int64), ("elem_offset", ctypes.c_int64),
         ("ordinal", ctypes.c_uint32), ("hyper", ctypes.c_int32),
         ("param_copy", ctypes.c_void_p),
-        ("copy_multicast", ctypes.c_int32), ("pad", ctypes.c_int32),
+        ("copy_multicast", ctypes.c_int32), ("grad_multicast", ctypes.c_int32),
     ]
 
 
@@ -97,6 +98,7 @@ SIGNATURES = {
     "aw4_dequantize_blocks": ([ctypes.POINTER(Scheme), _VP, _VP, _I64, _VP, _I32, _VP], _I32),
     "aw4_pack_codes": ([_VP, _I64, _VP, _I32, _VP], _I32),
     "aw4_unpack_codes": ([_VP, _I64, _VP, _I32, _VP], _I32),
+    "aw4_reduce_multicast": ([_VP, _I32, _I64, _F, _VP, _I32, _VP], _I32),
     "aw4_selfcheck_math": ([_VP, _I32, _VP], _I32),
 }
 

@@ -110,6 +110,20 @@ unpack_kernel(const uint8_t* packed, int64_t n, uint8_t* codes) {
         codes[i] = (packed[i >> 1] >> ((i & 1) * 4)) & 15;
 }
 
+// reduce_multicast(): out[8u .. 8u+7] = f32(sum over ranks) * scale, one
+// 8-value unit per thread step.
+template <int DT>
+__global__ void __launch_bounds__(kThreads)
+reduce_multicast_kernel(const void* mc, int64_t units, float scale, float* out) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t u = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; u < units; u += stride) {
+        float v[8];
+        load8_reduce<DT>(mc, 8 * u, v);
+        vmuls8(v, v, scale);
+        Elem<AW4_F32>::store8(out, 8 * u, v);
+    }
+}
+
 static int grid_1d(int device, int64_t work_items) {
     int sms = 0;
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
@@ -229,4 +243,35 @@ extern "C" int32_t aw4_unpack_codes(const uint8_t* packed, int64_t numel, uint8_
     note_launch();
     cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? AW4_OK : fail(AW4_ERR_CUDA, "unpack launch: %s", cudaGetErrorString(e));
+}
+
+extern "C" int32_t aw4_reduce_multicast(const void* mc, int32_t dtype, int64_t numel, float scale,
+                                        float* out, int32_t device, void* stream) {
+    if (numel < 0 || numel % 8)
+        return fail(AW4_ERR_INVALID, "aw4_reduce_multicast: numel must be a multiple of 8");
+    if (numel == 0) return AW4_OK;
+    if (!mc || !out || ((uintptr_t)mc % 16) || ((uintptr_t)out % 16))
+        return fail(AW4_ERR_INVALID, "aw4_reduce_multicast: null or misaligned buffer");
+    DeviceGuard guard(device);
+    if (!guard.ok()) return fail(AW4_ERR_CUDA, "cudaSetDevice(%d) failed", device);
+    const int64_t units = numel / 8;
+    const int grid = grid_1d(device, units);
+    cudaStream_t s = (cudaStream_t)stream;
+    switch (dtype) {
+    case AW4_F32:
+        reduce_multicast_kernel<AW4_F32><<<grid, kThreads, 0, s>>>(mc, units, scale, out);
+        break;
+    case AW4_BF16:
+        reduce_multicast_kernel<AW4_BF16><<<grid, kThreads, 0, s>>>(mc, units, scale, out);
+        break;
+    case AW4_F16:
+        reduce_multicast_kernel<AW4_F16><<<grid, kThreads, 0, s>>>(mc, units, scale, out);
+        break;
+    default:
+        return fail(AW4_ERR_INVALID, "aw4_reduce_multicast: bad dtype %d", dtype);
+    }
+    note_launch();
+    cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? AW4_OK
+                            : fail(AW4_ERR_CUDA, "reduce_multicast launch: %s", cudaGetErrorString(e));
 }

@@ -344,6 +344,49 @@ struct Elem<AW4_F16> {
     }
 };
 
+// 8 consecutive gradient values summed over the ranks of an NVSwitch
+// multicast object: `base` is the multicast address, and each 16-byte
+// multimem.ld_reduce returns the element-wise sum of every rank's copy,
+// reduced in the switch (BF16/F16 accumulated in FP32, then rounded to the
+// element type).  Relaxed, system scope: the caller orders it after the
+// ranks' writes with a cross-rank barrier.
+template <int DT>
+__device__ __forceinline__ void load8_reduce(const void* base, int64_t e, float v[8]);
+template <>
+__device__ __forceinline__ void load8_reduce<AW4_F32>(const void* base, int64_t e, float v[8]) {
+    const float* p = static_cast<const float*>(base) + e;
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v[0]), "=f"(v[1]), "=f"(v[2]), "=f"(v[3]) : "l"(p) : "memory");
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v[4]), "=f"(v[5]), "=f"(v[6]), "=f"(v[7]) : "l"(p + 4) : "memory");
+}
+template <>
+__device__ __forceinline__ void load8_reduce<AW4_BF16>(const void* base, int64_t e, float v[8]) {
+    const uint16_t* p = static_cast<const uint16_t*>(base) + e;
+    uint32_t w[4];
+    asm volatile(
+        "multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+        : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]) : "l"(p) : "memory");
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {   // element 2k in the low half
+        v[2 * k] = __uint_as_float(w[k] << 16);
+        v[2 * k + 1] = __uint_as_float(w[k] & 0xffff0000u);
+    }
+}
+template <>
+__device__ __forceinline__ void load8_reduce<AW4_F16>(const void* base, int64_t e, float v[8]) {
+    const uint16_t* p = static_cast<const uint16_t*>(base) + e;
+    uint32_t w[4];
+    asm volatile(
+        "multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.f16x2 {%0, %1, %2, %3}, [%4];"
+        : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]) : "l"(p) : "memory");
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        v[2 * k] = __half2float(__ushort_as_half((unsigned short)(w[k] & 0xffffu)));
+        v[2 * k + 1] = __half2float(__ushort_as_half((unsigned short)(w[k] >> 16)));
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Philox4x32-10 (Salmon, Moraes, Dror, Shaw, SC'11).  Counter layout:
 // (e/4 low word, e/4 high word, step, ordinal); key = 64-bit stream key;

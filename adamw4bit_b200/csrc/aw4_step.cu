@@ -57,8 +57,10 @@ struct KDesc {
     int32_t nblocks;
     int32_t tile_begin;
     uint32_t ordinal;
-    int32_t pc_multicast;   // pc is an NVLink multicast address (multimem stores)
+    int32_t flags;          // kPcMulticast | kGradMulticast
 };
+constexpr int32_t kPcMulticast = 1;     // pc is an NVLink multicast address (multimem stores)
+constexpr int32_t kGradMulticast = 2;   // grad is one: read the sum over ranks (ld_reduce)
 
 // One hyper-parameter set as the kernel reads it: the caller's aw4_hyper plus
 // host-derived constants of the fast denominator/update path (fast_bounds).
@@ -71,6 +73,7 @@ struct HyperDev {
     float m1_fast_max, m2_fast_max;               // lane bounds of the fast path (-1: off)
     uint32_t step;
     PhiloxKey m1_key, m2_key;                     // key schedules of the SR streams
+    float grad_scale;                             // multiplies multicast-reduced gradients
 };
 
 // One launch covers tensors of one hyper-parameter set, so every scalar is
@@ -163,7 +166,7 @@ __device__ __forceinline__ void update_ieee(float q[8], const float m1[8], const
 // model in symmetric memory, one multimem store to the NVLink multicast
 // address, which NVSwitch delivers to every rank's replica.
 __device__ __forceinline__ void store_model_copy(const KDesc& D, int64_t e0, const float p[8]) {
-    if (!D.pc_multicast) {
+    if (!(D.flags & kPcMulticast)) {
         Elem<AW4_BF16>::store8(D.pc, e0, p);
         return;
     }
@@ -227,7 +230,12 @@ step_kernel(const __grid_constant__ StepLaunch L) {
             float s1 = 0.0f, s2 = 0.0f;
             if (active) {
                 Elem<PT>::load8(D.param, e0, p);
-                Elem<GT>::load8(D.grad, e0, gr);
+                if (D.flags & kGradMulticast) {
+                    load8_reduce<GT>(D.grad, e0, gr);   // sum over ranks, in the switch
+                    vmuls8(gr, gr, H.grad_scale);
+                } else {
+                    Elem<GT>::load8(D.grad, e0, gr);
+                }
                 w1 = __ldcs(reinterpret_cast<const unsigned int*>(D.c1 + (e0 >> 1)));
                 w2 = __ldcs(reinterpret_cast<const unsigned int*>(D.c2 + (e0 >> 1)));
                 s1 = __ldcs(D.s1 + blk);
@@ -469,6 +477,7 @@ static HyperDev hyper_dev(const aw4_hyper& h, const aw4_scheme& m2s) {
     d.step = h.step;
     d.m1_key = philox_schedule(h.m1_key);
     d.m2_key = philox_schedule(h.m2_key);
+    d.grad_scale = h.grad_scale;
     d.pos_step = -h.neg_step;
     d.bsc = h.sqrt_bc2 * 0x1p24f;
     // float32 divisions on the host (SSE): correctly rounded
@@ -594,7 +603,8 @@ extern "C" int32_t aw4_step_quantized(const aw4_scheme* m1, const aw4_scheme* m2
                 d.d1 = t.m1_draws;
                 d.d2 = t.m2_draws;
                 d.pc = t.param_copy;
-                d.pc_multicast = (t.param_copy && t.copy_multicast) ? 1 : 0;
+                d.flags = ((t.param_copy && t.copy_multicast) ? kPcMulticast : 0) |
+                          (t.grad_multicast ? kGradMulticast : 0);
                 d.elem_offset = t.elem_offset;
                 d.nblocks = (int32_t)(t.numel / AW4_BLOCK);
                 d.tile_begin = L->n_tiles;

@@ -24,6 +24,19 @@ the multicast address (``multimem`` stores), which delivers it to every
 rank's replica while the kernel runs.  A symmetric-memory barrier ends the
 step.  Without multicast support the optimizer falls back to NCCL.
 
+With ``grad_reduce="multicast"`` (ZeRO-2) the gradients are not reduced
+beforehand: every rank's backward writes its local gradients into a buffer in
+symmetric memory (the optimizer binds each ``p.grad`` to a view of it), and
+the update kernel reads the sum over ranks of its own shard straight from
+the NVSwitch (``multimem.ld_reduce``: the switch adds the ranks' values), times
+``grad_scale`` (default 1/W, the mean).  The reduce-scatter is fused into the
+update: no reduced gradient is ever written to memory.  Together with
+``gather="multicast"`` one kernel per round does reduce-scatter, update and
+all-gather; the two collectives load opposite NVLink directions (the
+reduction reads from every GPU, the multicast stores write to every GPU).
+Symmetric-memory barriers before the update (all gradients written) and
+after it (all reads done before the next backward) bracket the step.
+
 Ownership is block-cyclic over ``rounds`` rounds: round i covers the flat
 range [i*W*c, (i+1)*W*c) and rank r owns its r-th c-element slice, so each
 round's all-gather writes one contiguous range and can run while the kernel
@@ -66,6 +79,19 @@ def _multicast_buffer(n: int, dtype, dev, group):
     if not mc:
         return None, None, 0
     return buf, handle, mc
+
+
+def grad_layout(plan_starts: list[int], padded: int, small_sizes: list[int]):
+    """Offsets of every gradient in the ZeRO-2 gradient buffer: the sharded
+    tensors at their flat-model offsets (plan_starts, inside [0, padded)),
+    the FP32-state tensors after them, each at an 8-value boundary (16 bytes,
+    the multimem.ld_reduce width).  Returns (sharded offsets, small offsets,
+    buffer length in values)."""
+    offs, off = [], padded
+    for n in small_sizes:
+        offs.append(off)
+        off += -(-n // 8) * 8
+    return list(plan_starts), offs, off
 
 
 class ShardPlan:
@@ -131,13 +157,21 @@ class ZeRO1AdamW4Bit:
         gather: ``"nccl"`` (all-gather on a side stream) or ``"multicast"``
             (the update kernel writes every replica through NVSwitch; needs
             ``master_weights`` and a process group of 2+ ranks).
+        grad_reduce: ``"local"`` (``p.grad`` holds already-reduced gradients)
+            or ``"multicast"`` (ZeRO-2: each ``p.grad`` is bound to this rank's
+            unreduced gradients in symmetric memory and the update reads the
+            sum over ranks through NVSwitch; needs 2+ ranks and multicast).
+        grad_dtype: dtype of the bound gradients (``grad_reduce="multicast"``;
+            default BF16).
+        grad_scale: factor on the summed gradients (default 1/W).
     """
 
     def __init__(self, params, *, recipe: str = "ze-eden", lr: float = 1e-3,
                  betas=(0.9, 0.95), eps: float = 1e-8, weight_decay: float = 0.1,
                  process_group=None, rounds: int = 4, quant_rng_seed: int = 0,
                  reserve_sms: int = 16, master_weights: bool = False,
-                 gather: str = "nccl"):
+                 gather: str = "nccl", grad_reduce: str = "local", grad_dtype=torch.bfloat16,
+                 grad_scale: float | None = None):
         self.all_params = [p for p in params]
         if not self.all_params:
             raise ValueError("ZeRO1AdamW4Bit needs parameters")
@@ -222,6 +256,13 @@ class ZeRO1AdamW4Bit:
             self.small.append(entry)
         self.step_count = 0
         self.segments = plan.segments
+        if grad_reduce not in ("local", "multicast"):
+            raise ValueError(f"unknown grad_reduce mode {grad_reduce!r}")
+        self.grad_reduce = grad_reduce
+        self.grad_scale = float(1.0 / W if grad_scale is None else grad_scale)
+        self.gsymm = None
+        if grad_reduce == "multicast":
+            self._bind_gradients(grad_dtype)
         nccl = W > 1 and self.gather_mode == "nccl"
         self.gather_stream = torch.cuda.Stream(dev) if nccl else None
         # With a concurrent all-gather, leave `reserve_sms` SMs free so NCCL's
@@ -232,6 +273,51 @@ class ZeRO1AdamW4Bit:
             self.symm.barrier(channel=0)   # every replica holds the initial model
         self.launch_timings: list | None = None
 
+    def _bind_gradients(self, grad_dtype) -> None:
+        """ZeRO-2: one symmetric-memory gradient buffer with a multicast
+        address, laid out by grad_layout; every p.grad becomes a view of it."""
+        if self.world < 2:
+            raise ValueError('grad_reduce="multicast" needs a process group of 2+ ranks')
+        if grad_dtype not in (torch.float32, torch.bfloat16, torch.float16):
+            raise ValueError(f"unsupported gradient dtype {grad_dtype}")
+        _, offs, off = grad_layout(self.plan.starts, self.padded,
+                                   [self.all_params[i].numel() for i in self.sindex])
+        gbuf, self.gsymm, self.gmc = _multicast_buffer(off, grad_dtype, self.device, self.group)
+        if not self.gmc:
+            raise RuntimeError('grad_reduce="multicast" needs NVSwitch multicast (symmetric '
+                               'memory with a multicast address), which this platform lacks')
+        gbuf.zero_()
+        self.gbuf, self.small_goff = gbuf, offs
+        self.small_gtotal = off - self.padded
+        self.small_g = torch.zeros(max(self.small_gtotal, 8), dtype=torch.float32,
+                                   device=self.device)
+        views = {}
+        for ti, i in enumerate(self.qindex):
+            s0 = self.plan.starts[ti]
+            views[i] = gbuf[s0:s0 + self.all_params[i].numel()]
+        for k, i in enumerate(self.sindex):
+            views[i] = gbuf[offs[k]:offs[k] + self.all_params[i].numel()]
+        for i, p in enumerate(self.all_params):
+            if p.dtype != grad_dtype and hasattr(p, "grad_dtype"):
+                p.grad_dtype = None   # a gradient dtype other than the parameter's
+            p.grad = views[i].view(p.shape)
+        self.gsymm.barrier(channel=0)
+
+    def zero_grad(self, set_to_none: bool = True) -> None:
+        """Zero the gradients.  With grad_reduce="multicast" the bound
+        buffer is zeroed in place (the bindings stay); otherwise the grads are
+        dropped (or zeroed when set_to_none is False)."""
+        if self.grad_reduce == "multicast":
+            self.gbuf.zero_()
+            return
+        for p in self.all_params:
+            if p.grad is None:
+                continue
+            if set_to_none:
+                p.grad = None
+            else:
+                p.grad.zero_()
+
     @torch.no_grad()
     def step(self) -> None:
         self.step_count += 1
@@ -240,17 +326,20 @@ class ZeRO1AdamW4Bit:
                            SCHEMES[self.m2].next_bias)
         harr = (N.Hyper * 1)(N.Hyper(hy["w1"], hy["w2"], hy["decay"], hy["neg_step"],
                                      hy["sqrt_bc2"], hy["eps"], hy["sr_bias"], t, self.keys[0],
-                                     self.keys[1]))
+                                     self.keys[1], self.grad_scale))
         dev = self.device
         cur = torch.cuda.current_stream(dev)
         pdt = N.DTYPE_CODES[torch.float32 if self.master_weights else self.dtype]
         esz_p = self.flat.element_size()
+        reduce_mc = self.grad_reduce == "multicast"
         grads = [p.grad for p in self.params]
         if any(g is None for g in grads) or any(self.all_params[i].grad is None
                                                 for i in self.sindex):
             raise RuntimeError("ZeRO1AdamW4Bit.step needs a gradient for every parameter")
-        gdt = N.DTYPE_CODES[grads[0].dtype]
+        gdt = N.DTYPE_CODES[self.gbuf.dtype if reduce_mc else grads[0].dtype]
         W = self.world
+        if reduce_mc:
+            self.gsymm.barrier(channel=0)   # every rank's gradients are written
         for r, segs in enumerate(self.segments):
             descs = []
             for ti, s, n, so in segs:
@@ -264,13 +353,17 @@ class ZeRO1AdamW4Bit:
                     target, copy = self.master.data_ptr() + so * 4, model
                 else:
                     target, copy = model, None
+                if reduce_mc:   # the sum over ranks, read through NVSwitch
+                    gptr = self.gmc + (self.plan.starts[ti] + s) * self.gbuf.element_size()
+                else:
+                    gptr = g.data_ptr() + s * g.element_size()
                 descs.append(N.QTensor(
-                    target, g.data_ptr() + s * g.element_size(),
+                    target, gptr,
                     self.m1_codes.data_ptr() + so // 2, self.m1_scales.data_ptr() + (so // 128) * 4,
                     self.m2_codes.data_ptr() + so // 2, self.m2_scales.data_ptr() + (so // 128) * 4,
                     # Philox ordinal: the position among all parameters, as in
                     # the single-GPU optimizer, so SR draws do not depend on sharding
-                    None, None, n, s, self.qindex[ti], 0, copy, multicast))
+                    None, None, n, s, self.qindex[ti], 0, copy, multicast, int(reduce_mc)))
             if descs:
                 arr = (N.QTensor * len(descs))(*descs)
                 if self.launch_timings is not None:
@@ -294,10 +387,14 @@ class ZeRO1AdamW4Bit:
         self._step_small(harr, cur)
         if W > 1 and self.gather_mode == "nccl":
             cur.wait_stream(self.gather_stream)
-        elif self.symm is not None:
+        if self.symm is not None:
             # every rank's multimem stores are in every replica once all
             # ranks' update kernels have completed
             self.symm.barrier(channel=0)
+        elif reduce_mc:
+            # no rank's next backward overwrites gradients another rank is
+            # still reading
+            self.gsymm.barrier(channel=0)
 
     def _step_small(self, harr, cur) -> None:
         """The FP32-state update of the small tensors, identical on every rank
@@ -306,12 +403,27 @@ class ZeRO1AdamW4Bit:
             return
         dev = self.device
         pdt = N.DTYPE_CODES[torch.float32 if self.master_weights else self.dtype]
-        gdt = N.DTYPE_CODES[self.all_params[self.sindex[0]].grad.dtype]
+        reduce_mc = self.grad_reduce == "multicast"
+        if reduce_mc:
+            # the small tensors' summed gradients, read through NVSwitch into FP32
+            esz = self.gbuf.element_size()
+            N.check(N.lib().aw4_reduce_multicast(self.gmc + self.padded * esz,
+                                                 N.DTYPE_CODES[self.gbuf.dtype],
+                                                 self.small_gtotal, self.grad_scale,
+                                                 N.ptr(self.small_g), dev.index, cur.cuda_stream),
+                    "aw4_reduce_multicast")
+            gdt = N.DTYPE_CODES[torch.float32]
+        else:
+            gdt = N.DTYPE_CODES[self.all_params[self.sindex[0]].grad.dtype]
         descs, keep = [], []
-        for i, st in zip(self.sindex, self.small):
+        for k, (i, st) in enumerate(zip(self.sindex, self.small)):
             p = self.all_params[i]
             target = st["master"] if self.master_weights else p
-            g = p.grad.contiguous()
+            if reduce_mc:
+                o = self.small_goff[k] - self.padded
+                g = self.small_g[o:o + p.numel()]
+            else:
+                g = p.grad.contiguous()
             keep.append(g)
             descs.append(N.FTensor(target.data_ptr(), g.data_ptr(),
                                    st["m1"].data_ptr(), st["m2"].data_ptr(), p.numel(), 0, 0))

@@ -312,12 +312,17 @@ def run_ours(args, rank, world, local):
         # BF16 (written by the update kernel) and the all-gather moves 2 B/value
         opt = ZeRO1AdamW4Bit(params, recipe=args.recipe, rounds=args.rounds,
                              master_weights=master, reserve_sms=args.reserve_sms,
-                             gather="multicast" if args.gather == "multicast" else "nccl")
+                             gather="multicast" if args.gather == "multicast" else "nccl",
+                             grad_reduce=args.grad_reduce)
         step_fn = opt.step
         updated_per_rank = opt.owned_numel()
     b_per_elem = B_PER_ELEM + (2 if master else 0)   # + the BF16 model copy write
+    zero2 = world > 1 and args.grad_reduce == "multicast"
     for p, g in zip(params, grads):
-        p.grad = g
+        if zero2:   # this rank's unreduced gradients, in the bound symmetric buffer
+            p.grad.copy_(g)
+        else:
+            p.grad = g
     for _ in range(args.warmup):
         step_fn()
     barrier(world)
@@ -384,8 +389,12 @@ def run_ours(args, rank, world, local):
                            "param_dtype": "fp32 master + bf16 model copy" if master else "fp32",
                            "grad_dtype": "bf16", "recipe": args.recipe.upper(),
                            "parallelism": "single GPU" if world == 1 else
-                           f"zero1-dp{world}, {'bf16 model' if master else 'fp32'} gather "
-                           f"({getattr(opt, 'gather_mode', 'nccl')})",
+                           f"{'zero2' if zero2 else 'zero1'}-dp{world}, "
+                           f"{'bf16 model' if master else 'fp32'} gather "
+                           f"({getattr(opt, 'gather_mode', 'nccl')})"
+                           + (", gradient reduce-scatter fused into the update "
+                              "(multimem.ld_reduce)" if zero2 else
+                              ", gradients already reduced"),
                            "l2": "no flush: 56 GB working set >> 126 MB L2"},
                 "roofline": roofline,
                 "update_only": {"values_per_rank": updated_per_rank,
@@ -394,6 +403,17 @@ def run_ours(args, rank, world, local):
                                     updated_per_rank * args.steps / (kernel_ms_max / 1e3)},
                 "clocks": clocks, "gpu_launches": int(launches),
                 "e2e": e2e}
+        if zero2:
+            # per GPU and step, each NVLink direction carries 2 B per value:
+            # out, its gradients to the switch's reductions of every shard
+            # ((W-1)/W) and its shard's multicast model stores (1/W); in, the
+            # reduced sums of its shard (1/W) and the other shards' model
+            # values ((W-1)/W)
+            nv = 2.0 * total
+            line["nvlink"] = {"bytes_per_direction_per_gpu": nv,
+                              "achieved_gbs": round(nv / (ms_per_step / 1e3) / 1e9, 1),
+                              "peak_gbs": 770.0, "peak_source": "measured peer copy, per direction",
+                              "frac": round(nv / (ms_per_step / 1e3) / 1e9 / 770.0, 4)}
         if world == 1 and args.cpu_sample > 0:
             line["cpu_baseline"] = {k: v for k, v in cpu_oracle_rate(
                 args.cpu_sample, args.cpu_steps).items() if k != "seconds_per_step"}
@@ -437,6 +457,8 @@ def run_e2e_sharded(args, opt, params, grads, dev, world, total):
     pinned host memory, steps (update + NCCL all-gather), and copies its
     updated parameter shard back to pinned host memory."""
     segs = [seg for round_segs in opt.segments for seg in round_segs]
+    if opt.grad_reduce == "multicast":   # ZeRO-2: every rank brings its full local gradients
+        segs = [(ti, 0, p.numel(), 0) for ti, p in enumerate(params)]
     host_g = [grads[ti].reshape(-1)[s:s + n].to("cpu").pin_memory() for ti, s, n, _ in segs]
     owned = [(a, b) for a, b in opt.owned if b > a]
     host_p = [torch.empty(b - a, dtype=opt.flat.dtype, pin_memory=True) for a, b in owned]
@@ -478,6 +500,9 @@ def main():
     ap.add_argument("--rounds", type=int, default=4, help="ZeRO-1 gather rounds")
     ap.add_argument("--recipe", choices=["ze-eden", "zip-sr"], default="ze-eden",
                     help="the optimizer recipe (BASELINE config 5 is ZE-EDEN)")
+    ap.add_argument("--grad-reduce", choices=["local", "multicast"], default="local",
+                    help="N>1: gradients already reduced (local), or ZeRO-2 with the "
+                         "reduce-scatter fused into the update through NVSwitch (multicast)")
     ap.add_argument("--reserve-sms", type=int, default=16,
                     help="N>1: SMs the update grid leaves to the concurrent all-gather")
     ap.add_argument("--gather", choices=["multicast", "bf16", "fp32"], default="bf16",

@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define AW4_ABI_VERSION 3
+#define AW4_ABI_VERSION 4
 #define AW4_BLOCK 128          /* elements per quantization block (4-bit default) */
 #define AW4_LUT_BINS 1024      /* maximum uniform bins over [-1, 1] for the rounding search */
 
@@ -82,11 +82,16 @@ typedef struct aw4_scheme {
  *   w1 = f32(1 - beta1)        w2 = f32(1 - beta2)
  *   decay = f32(1 - lr * wd)   neg_step = f32(-lr / (1 - beta1^t))
  *   sqrt_bc2 = f32(sqrt(1 - beta2^t))          eps = f32(eps)
- *   sr_bias = f32(max(storage bias correction, 1e-12))  (update SR only)  */
+ *   sr_bias = f32(max(storage bias correction, 1e-12))  (update SR only)
+ * grad_scale multiplies gradients read through a multicast address
+ * (aw4_qtensor.grad_multicast), e.g. 1/W to average over W ranks; other
+ * gradients are used as given. */
 typedef struct aw4_hyper {
     float w1, w2, decay, neg_step, sqrt_bc2, eps, sr_bias;
     uint32_t step;                 /* t, 1-based: Philox counter word */
     uint64_t m1_key, m2_key;       /* Philox keys of the m1 / m2 SR streams */
+    float grad_scale;
+    int32_t pad;                   /* zero */
 } aw4_hyper;
 
 /* One quantized tensor (or one contiguous shard of it, for ZeRO-1). */
@@ -110,7 +115,13 @@ typedef struct aw4_qtensor {
                                     * (an NVSwitch multicast object bound on every rank);
                                     * the copy is written with multimem stores and lands
                                     * in every rank's replica */
-    int32_t pad;
+    int32_t grad_multicast;        /* nonzero: grad is an NVLink multicast address of a
+                                    * gradient buffer bound on every rank; the kernel reads
+                                    * the sum over ranks (multimem.ld_reduce: the switch
+                                    * adds the ranks' values, BF16/F16 accumulated in FP32
+                                    * and rounded to the gradient dtype) times the hyper
+                                    * set's grad_scale (ZeRO-2: the gradient reduce-scatter
+                                    * fused into the update) */
 } aw4_qtensor;
 
 /* One tensor with FP32 moments (numel arbitrary). */
@@ -175,6 +186,15 @@ int32_t aw4_pack_codes(const uint8_t* codes, int64_t numel, uint8_t* packed,
                        int32_t device, void* stream);
 int32_t aw4_unpack_codes(const uint8_t* packed, int64_t numel, uint8_t* codes,
                          int32_t device, void* stream);
+
+/* Reads the sum over ranks of a gradient buffer through its NVLink multicast
+ * address (multimem.ld_reduce, the same reduction as grad_multicast) and
+ * writes out[i] = f32(sum[i]) * scale.  numel a multiple of 8; mc 16-byte
+ * aligned; dtype AW4_F32, AW4_BF16 or AW4_F16.  ZeRO-2 uses it for the
+ * tensors that keep FP32 moments.  No reference counterpart: the reference
+ * has no data parallelism. */
+int32_t aw4_reduce_multicast(const void* mc, int32_t dtype, int64_t numel, float scale,
+                             float* out, int32_t device, void* stream);
 
 /* Exhaustive device check of the reciprocal and square root the step kernel
  * builds from the hardware approximations, against IEEE round-to-nearest, over

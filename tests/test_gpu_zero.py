@@ -238,3 +238,108 @@ def test_zero1_shard_state_dict_round_trip_with_master_weights():
                          rounds=3, master_weights=True, quant_rng_seed=4)
     with pytest.raises(ValueError, match="different sharding"):
         bad.load_state_dict(sd)
+
+
+def _rank_grad(shape, step, index, rank):
+    """Rank `rank`'s BF16 gradient of parameter `index` at `step`: integers
+    in [-255, 255] times 2^-12, exact in BF16, so the switch's FP32 sum over
+    ranks is exact and its BF16 rounding is the only rounding."""
+    g = torch.Generator().manual_seed(100_000 * step + 100 * index + rank)
+    k = torch.randint(-255, 256, shape, generator=g).float()
+    return (k * 2.0 ** -12).to(torch.bfloat16)
+
+
+def _worker_reduce(rank, world, port, recipe, master, gather, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import datetime
+
+    import torch.distributed as dist
+
+    from adamw4bit_b200 import ZEEDENAdamW4Bit, ZIPSRAdamW4Bit
+    from adamw4bit_b200.zero import ZeRO1AdamW4Bit
+    try:
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=120), device_id=dev)
+        vals, _ = _make(dev)
+        if master:
+            vals = [v.to(torch.bfloat16).float() for v in vals]
+        model_dtype = torch.bfloat16 if master else torch.float32
+        params = [torch.nn.Parameter(v.clone().to(model_dtype)) for v in vals]
+        for p in params:
+            p.grad_dtype = None
+        try:
+            opt = ZeRO1AdamW4Bit(params, recipe=recipe, rounds=2, quant_rng_seed=9,
+                                 master_weights=master, gather=gather, grad_reduce="multicast")
+        except RuntimeError as e:
+            if "multicast" in str(e):
+                q.put((rank, True, "skip: no NVSwitch multicast on this platform"))
+                return
+            raise
+        if opt.gather_mode != gather:
+            q.put((rank, True, "skip: no NVSwitch multicast on this platform"))
+            return
+        steps = 3
+        for t in range(steps):
+            opt.zero_grad()
+            for i, p in enumerate(params):
+                p.grad.copy_(_rank_grad(p.shape, t, i, rank).to(dev))
+            opt.step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        # single-GPU reference fed the FP32 gradients the fused read defines:
+        # f32(bf16(sum over ranks)) / world
+        ref = [torch.nn.Parameter(v.clone()) for v in vals]
+        cls = ZEEDENAdamW4Bit if recipe == "ze-eden" else ZIPSRAdamW4Bit
+        single = cls(ref, quant_rng_seed=9)
+        for t in range(steps):
+            for i, p in enumerate(ref):
+                s = sum(_rank_grad(p.shape, t, i, r).float() for r in range(world))
+                p.grad = (s.to(torch.bfloat16).float() * (1.0 / world)).to(dev)
+            single.step()
+        torch.cuda.synchronize()
+        cons = opt.state_dict(consolidated=True)
+        ok = _same_state(cons, single.state_dict())
+        why = None if ok else "state"
+        if master:
+            okp = all(torch.equal(a.detach().view(torch.int16),
+                                  b.detach().to(torch.bfloat16).view(torch.int16))
+                      for a, b in zip(params, ref))
+        else:
+            okp = all(torch.equal(a.detach().view(torch.int32), b.detach().view(torch.int32))
+                      for a, b in zip(params, ref))
+        if not okp:
+            why = (why or "") + " params"
+        torch.cuda.synchronize()
+        dist.barrier()
+        q.put((rank, ok and okp, why))
+    except Exception as e:  # report to the parent instead of hanging it
+        q.put((rank, False, repr(e)))
+    finally:
+        if dist.is_initialized():
+            torch.cuda.synchronize()
+            dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("recipe,master,gather", [
+    ("ze-eden", True, "multicast"), ("zip-sr", True, "multicast"), ("ze-eden", False, "nccl")])
+def test_zero2_fused_reduce_two_gpus_matches_single_gpu(recipe, master, gather):
+    """ZeRO-2: the update kernel reads the gradient sum over ranks through
+    NVSwitch (multimem.ld_reduce) and must equal the single-GPU step fed
+    f32(bf16(sum)) / W, bit for bit."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 30100 + (os.getpid() % 400) + (7 if master else 0) + (3 if recipe == "zip-sr" else 0)
+    procs = [ctx.Process(target=_worker_reduce, args=(r, 2, port, recipe, master, gather, q))
+             for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    if all(msg and str(msg).startswith("skip") for _, _, msg in results):
+        pytest.skip(results[0][2])
+    assert all(ok for _, ok, _ in results), results

@@ -17,7 +17,7 @@ import torch.multiprocessing as mp
 from adamw4bit_b200 import AdamW8bit, QuantizedAdamW, ZEEDENAdamW4Bit, ZIPSRAdamW4Bit
 from adamw4bit_b200.optimizer import hyper_scalars
 from adamw4bit_b200.quantization import QuantState, default_block_size, is_4bit_scheme
-from adamw4bit_b200.zero import ShardPlan
+from adamw4bit_b200.zero import ShardPlan, grad_layout
 
 
 def _p(n=4096):
@@ -193,6 +193,22 @@ def test_shard_plan_covers_every_value_once(world, rounds):
                 offs.add(so)
                 assert so + n <= plan.state_numel()
     assert (seen == 1).all()
+
+
+def test_zero2_grad_layout_is_disjoint_and_aligned():
+    """ZeRO-2 gradient buffer: sharded tensors at their flat-model offsets,
+    the FP32-state tensors after the padded model, each at a 16-byte
+    (8-value) boundary, no overlaps."""
+    sizes = [4096, 128 * 96, 8192]
+    plan = ShardPlan(sizes, 2, 0, 2)
+    small = [768, 300, 5, 8]
+    qoffs, soffs, total = grad_layout(plan.starts, plan.padded, small)
+    assert qoffs == plan.starts
+    spans = [(o, o + n) for o, n in zip(qoffs, sizes)] + [(o, o + n) for o, n in zip(soffs, small)]
+    spans.sort()
+    assert all(a[1] <= b[0] for a, b in zip(spans, spans[1:]))
+    assert all(o % 8 == 0 for o in soffs) and soffs[0] >= plan.padded
+    assert total % 8 == 0 and total >= soffs[-1] + small[-1]
 
 
 def _gloo_worker(rank, world, port, q):

@@ -39,7 +39,7 @@ def test_library_loads_and_exports_every_declared_symbol():
 def test_struct_layouts_match_header():
     # sizes follow from the C declarations (natural alignment, x86-64)
     assert ctypes.sizeof(N.Scheme) == 64 + 12 + N.LUT_BINS + 72 + 8 + 4
-    assert ctypes.sizeof(N.Hyper) == 48
+    assert ctypes.sizeof(N.Hyper) == 56
     assert ctypes.sizeof(N.QTensor) == 104
     assert ctypes.sizeof(N.FTensor) == 48
 
