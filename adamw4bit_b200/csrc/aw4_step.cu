@@ -57,10 +57,9 @@ struct KDesc {
     int32_t nblocks;
     int32_t tile_begin;
     uint32_t ordinal;
-    int32_t flags;          // kPcMulticast | kGradMulticast
+    int32_t flags;          // kPcMulticast
 };
 constexpr int32_t kPcMulticast = 1;     // pc is an NVLink multicast address (multimem stores)
-constexpr int32_t kGradMulticast = 2;   // grad is one: read the sum over ranks (ld_reduce)
 
 // One hyper-parameter set as the kernel reads it: the caller's aw4_hyper plus
 // host-derived constants of the fast denominator/update path (fast_bounds).
@@ -194,7 +193,9 @@ __device__ __forceinline__ void load_uniforms(float u[8], const float* draws,
     }
 }
 
-template <int PT, int GT, int M1, int M2>
+// GMC: the launch's gradients are multicast addresses (ZeRO-2), read as the
+// sum over ranks; a separate instantiation keeps the plain load branch-free.
+template <int PT, int GT, int M1, int M2, bool GMC>
 __global__ void __launch_bounds__(kThreads, 4)
 step_kernel(const __grid_constant__ StepLaunch L) {
     __shared__ __align__(16) StepSmem sm;
@@ -230,8 +231,8 @@ step_kernel(const __grid_constant__ StepLaunch L) {
             float s1 = 0.0f, s2 = 0.0f;
             if (active) {
                 Elem<PT>::load8(D.param, e0, p);
-                if (D.flags & kGradMulticast) {
-                    load8_reduce<GT>(D.grad, e0, gr);   // sum over ranks, in the switch
+                if (GMC) {   // grad is a multicast address: the sum over ranks
+                    load8_reduce<GT>(D.grad, e0, gr);
                     vmuls8(gr, gr, H.grad_scale);
                 } else {
                     Elem<GT>::load8(D.grad, e0, gr);
@@ -406,32 +407,37 @@ __global__ void __launch_bounds__(kThreads) fp32_state_kernel(const __grid_const
 // ---------------------------------------------------------------------------
 using StepFn = void (*)(StepLaunch);
 
-template <int PT, int GT, int M1>
+template <int PT, int GT, int M1, bool GMC>
 static StepFn pick_m2(int m2) {
     switch (m2) {
-    case AW4_RTN: return step_kernel<PT, GT, M1, AW4_RTN>;
-    case AW4_SR_VALUE: return step_kernel<PT, GT, M1, AW4_SR_VALUE>;
-    case AW4_SR_UPDATE: return step_kernel<PT, GT, M1, AW4_SR_UPDATE>;
+    case AW4_RTN: return step_kernel<PT, GT, M1, AW4_RTN, GMC>;
+    case AW4_SR_VALUE: return step_kernel<PT, GT, M1, AW4_SR_VALUE, GMC>;
+    case AW4_SR_UPDATE: return step_kernel<PT, GT, M1, AW4_SR_UPDATE, GMC>;
     }
     return nullptr;
 }
 
-template <int PT, int GT>
+template <int PT, int GT, bool GMC>
 static StepFn pick_m1(int m1, int m2) {
-    if (m1 == AW4_RTN) return pick_m2<PT, GT, AW4_RTN>(m2);
-    if (m1 == AW4_SR_VALUE) return pick_m2<PT, GT, AW4_SR_VALUE>(m2);
+    if (m1 == AW4_RTN) return pick_m2<PT, GT, AW4_RTN, GMC>(m2);
+    if (m1 == AW4_SR_VALUE) return pick_m2<PT, GT, AW4_SR_VALUE, GMC>(m2);
+    return nullptr;
+}
+
+template <bool GMC>
+static StepFn pick_dtypes(int pdt, int gdt, int m1, int m2) {
+    if (pdt == AW4_F32 && gdt == AW4_F32) return pick_m1<AW4_F32, AW4_F32, GMC>(m1, m2);
+    if (pdt == AW4_F32 && gdt == AW4_BF16) return pick_m1<AW4_F32, AW4_BF16, GMC>(m1, m2);
+    if (pdt == AW4_F32 && gdt == AW4_F16) return pick_m1<AW4_F32, AW4_F16, GMC>(m1, m2);
+    if (pdt == AW4_BF16 && gdt == AW4_BF16) return pick_m1<AW4_BF16, AW4_BF16, GMC>(m1, m2);
+    if (pdt == AW4_F16 && gdt == AW4_F16) return pick_m1<AW4_F16, AW4_F16, GMC>(m1, m2);
     return nullptr;
 }
 
 // Supported (param, grad) dtype pairs: equal dtypes, or FP32 master params
-// with BF16/FP16 gradients.
-static StepFn pick_step(int pdt, int gdt, int m1, int m2) {
-    if (pdt == AW4_F32 && gdt == AW4_F32) return pick_m1<AW4_F32, AW4_F32>(m1, m2);
-    if (pdt == AW4_F32 && gdt == AW4_BF16) return pick_m1<AW4_F32, AW4_BF16>(m1, m2);
-    if (pdt == AW4_F32 && gdt == AW4_F16) return pick_m1<AW4_F32, AW4_F16>(m1, m2);
-    if (pdt == AW4_BF16 && gdt == AW4_BF16) return pick_m1<AW4_BF16, AW4_BF16>(m1, m2);
-    if (pdt == AW4_F16 && gdt == AW4_F16) return pick_m1<AW4_F16, AW4_F16>(m1, m2);
-    return nullptr;
+// with BF16/FP16 gradients; gmc selects the multicast-reduced gradient read.
+static StepFn pick_step(int pdt, int gdt, int m1, int m2, bool gmc) {
+    return gmc ? pick_dtypes<true>(pdt, gdt, m1, m2) : pick_dtypes<false>(pdt, gdt, m1, m2);
 }
 
 using FFn = void (*)(FLaunch);
@@ -527,7 +533,7 @@ extern "C" int32_t aw4_step_quantized(const aw4_scheme* m1, const aw4_scheme* m2
         return fail(AW4_ERR_UNSUPPORTED, "aw4_step_quantized: m1 rounding must be RTN or value SR");
     if (m2->round_mode < AW4_RTN || m2->round_mode > AW4_SR_UPDATE)
         return fail(AW4_ERR_INVALID, "aw4_step_quantized: bad m2 rounding mode");
-    StepFn fn = pick_step(param_dtype, grad_dtype, m1->round_mode, m2->round_mode);
+    StepFn fn = pick_step(param_dtype, grad_dtype, m1->round_mode, m2->round_mode, false);
     if (!fn)
         return fail(AW4_ERR_UNSUPPORTED,
                     "aw4_step_quantized: unsupported (param, grad) dtype pair %d/%d", param_dtype,
@@ -561,14 +567,16 @@ extern "C" int32_t aw4_step_quantized(const aw4_scheme* m1, const aw4_scheme* m2
     int grid_cap = grid_for(fn, device, 1 << 30);
     if (max_ctas > 0) grid_cap = std::min(grid_cap, max_ctas);
 
-    // Distinct hyper-parameter sets (equal contents count as one), then one
-    // or more launches of <= kMaxTensors tensors per set.
+    // Distinct (hyper-parameter set, gradient kind) pairs (equal hyper
+    // contents count as one), then one or more launches of <= kMaxTensors
+    // tensors per pair.
     std::vector<int> set_of(n_tensors, -1), reps;
     for (int i = 0; i < n_tensors; ++i) {
         for (size_t k = 0; k < reps.size(); ++k)
-            if (tensors[reps[k]].hyper == tensors[i].hyper ||
-                std::memcmp(&hypers[tensors[reps[k]].hyper], &hypers[tensors[i].hyper],
-                            sizeof(aw4_hyper)) == 0) {
+            if ((tensors[reps[k]].grad_multicast != 0) == (tensors[i].grad_multicast != 0) &&
+                (tensors[reps[k]].hyper == tensors[i].hyper ||
+                 std::memcmp(&hypers[tensors[reps[k]].hyper], &hypers[tensors[i].hyper],
+                             sizeof(aw4_hyper)) == 0)) {
                 set_of[i] = (int)k;
                 break;
             }
@@ -586,6 +594,11 @@ extern "C" int32_t aw4_step_quantized(const aw4_scheme* m1, const aw4_scheme* m2
     int32_t rc = AW4_OK;
     for (size_t set = 0; set < reps.size() && rc == AW4_OK; ++set) {
         L->h = hyper_dev(hypers[tensors[reps[set]].hyper], *m2);
+        // same resources as fn (launch bounds, shared memory): same grid cap
+        const StepFn sfn = tensors[reps[set]].grad_multicast
+                               ? pick_step(param_dtype, grad_dtype, m1->round_mode,
+                                           m2->round_mode, true)
+                               : fn;
         int i = 0;
         while (i < n_tensors && rc == AW4_OK) {
             L->n_tensors = 0;
@@ -603,8 +616,7 @@ extern "C" int32_t aw4_step_quantized(const aw4_scheme* m1, const aw4_scheme* m2
                 d.d1 = t.m1_draws;
                 d.d2 = t.m2_draws;
                 d.pc = t.param_copy;
-                d.flags = ((t.param_copy && t.copy_multicast) ? kPcMulticast : 0) |
-                          (t.grad_multicast ? kGradMulticast : 0);
+                d.flags = (t.param_copy && t.copy_multicast) ? kPcMulticast : 0;
                 d.elem_offset = t.elem_offset;
                 d.nblocks = (int32_t)(t.numel / AW4_BLOCK);
                 d.tile_begin = L->n_tiles;
@@ -618,7 +630,7 @@ extern "C" int32_t aw4_step_quantized(const aw4_scheme* m1, const aw4_scheme* m2
             }
             if (rc != AW4_OK || L->n_tensors == 0) break;
             const int grid = std::min(grid_cap, L->n_tiles);
-            fn<<<grid, kThreads, 0, s>>>(*L);
+            sfn<<<grid, kThreads, 0, s>>>(*L);
             note_launch();
             cudaError_t e = cudaGetLastError();
             if (e != cudaSuccess) rc = fail(AW4_ERR_CUDA, "step launch: %s", cudaGetErrorString(e));
