@@ -301,6 +301,7 @@ class ZeRO1AdamW4Bit:
             if p.dtype != grad_dtype and hasattr(p, "grad_dtype"):
                 p.grad_dtype = None   # a gradient dtype other than the parameter's
             p.grad = views[i].view(p.shape)
+        self.grad_ptrs = [p.grad.data_ptr() for p in self.all_params]
         self.gsymm.barrier(channel=0)
 
     def zero_grad(self, set_to_none: bool = True) -> None:
@@ -320,6 +321,14 @@ class ZeRO1AdamW4Bit:
 
     @torch.no_grad()
     def step(self) -> None:
+        if self.grad_reduce == "multicast" and any(
+                p.grad is None or p.grad.data_ptr() != ptr
+                for p, ptr in zip(self.all_params, self.grad_ptrs)):
+            # a p.grad replaced or set to None (e.g. by module.zero_grad())
+            # no longer lands in the buffer the kernel reads
+            raise RuntimeError('grad_reduce="multicast": a parameter\'s .grad is no longer '
+                               'the bound view; zero gradients with the optimizer\'s '
+                               'zero_grad(), not by setting them to None')
         self.step_count += 1
         t = self.step_count
         hy = hyper_scalars(self.lr, self.betas[0], self.betas[1], self.eps, self.wd, t,
