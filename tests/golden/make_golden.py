@@ -1,10 +1,10 @@
 """Generate the golden fixtures in tests/golden/ by running the REFERENCE.
 
-Run in a container that has the reference checkout (nubank/adamw4bit) at
-``--reference`` (default /root/reference); the fixtures are committed so the
-tests never need the reference at run time:
+Run where a checkout of the reference (nubank/adamw4bit) exists, passing its
+root as ``--reference``; the fixtures are committed so the tests never need
+the reference at run time:
 
-    python tests/golden/make_golden.py --reference /root/reference
+    python tests/golden/make_golden.py --reference <path to the reference checkout>
 
 Every optimizer trajectory uses the reference's eager path (optimized=False),
 the parity oracle named by the survey.  Inputs are seeded synthetic tensors
@@ -189,7 +189,7 @@ def codec_cases(quant) -> None:
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="root of the reference checkout")
     ap.add_argument("--skip-full", action="store_true", help="skip the 16.8M-element runs")
     args = ap.parse_args()
     sys.path.insert(0, os.path.join(args.reference, "src"))
