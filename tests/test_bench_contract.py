@@ -1,0 +1,43 @@
+"""bench.py's contract, checked without a GPU: the benchmark's parameter set
+is Llama-3-8B as the workload names it, and the CPU reference arm prints one
+JSON line with the keys the measurement driver reads."""
+
+from __future__ import annotations
+
+import json
+import os
+import subprocess
+import sys
+
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+import bench  # noqa: E402
+
+
+def test_llama3_8b_parameter_set():
+    shapes = bench.llama3_8b_shapes()
+    assert len(shapes) == 291
+    assert sum(int(torch.Size(s).numel()) for s in shapes) == 8_030_261_248
+    # every tensor qualifies for 4-bit state (numel >= 4096, multiple of 128)
+    assert all(torch.Size(s).numel() >= 4096 and torch.Size(s).numel() % 128 == 0 for s in shapes)
+
+
+def test_reference_arm_prints_one_contract_line():
+    out = subprocess.run(
+        [sys.executable, "bench.py", "--impl", "reference", "--steps", "1", "--warmup", "0",
+         "--cpu-sample", str(1 << 20)],
+        cwd=ROOT, capture_output=True, text=True, timeout=600, check=True)
+    lines = [ln for ln in out.stdout.splitlines() if ln.startswith("{")]
+    assert len(lines) == 1
+    rec = json.loads(lines[0])
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step",
+                "higher_is_better", "scaling", "vs_baseline", "dtype", "data", "config",
+                "cpu_baseline", "e2e"):
+        assert key in rec, key
+    assert rec["impl"] == "reference" and rec["metric"] == bench.METRIC
+    assert rec["value"] > 0 and rec["higher_is_better"] is True
+    assert rec["e2e"]["h2d_bytes_per_step"] == 0 and rec["e2e"]["d2h_bytes_per_step"] == 0
+    assert rec["cpu_baseline"]["kind"] in ("port", "reference")
