@@ -422,19 +422,32 @@ def run_ours(args, rank, world, local):
 
 def run_e2e(args, opt, params, grads, dev, world, total):
     """Public-API step with host buffers: pinned grads -> device, step,
-    updated params -> pinned host, all inside the timed region."""
+    updated params -> pinned host, all inside the timed region.  The
+    read-back of step t's parameters runs on a second stream and overlaps the
+    upload of step t+1's gradients (PCIe carries both directions at once);
+    step t+1's update waits for that read-back before it overwrites the
+    parameters, and the timed region ends after the last read-back."""
     host_g = [g.detach().to("cpu").pin_memory() for g in grads]
     host_p = [torch.empty(p.shape, dtype=p.dtype, pin_memory=True) for p in params]
     h2d = sum(g.numel() * g.element_size() for g in host_g)
     d2h = sum(p.numel() * p.element_size() for p in host_p)
     cur = torch.cuda.current_stream(dev)
+    side = torch.cuda.Stream(dev)
+    read_back = torch.cuda.Event()
+    read_back.record(side)          # created and complete: nothing to wait for yet
 
     def one():
         for p, hg in zip(params, host_g):
             p.grad.copy_(hg, non_blocking=True)
+        cur.wait_event(read_back)   # the previous step's parameters are on the host
         opt.step()
-        for p, hp in zip(params, host_p):
-            hp.copy_(p.detach(), non_blocking=True)
+        stepped = torch.cuda.Event()
+        stepped.record(cur)
+        side.wait_event(stepped)
+        with torch.cuda.stream(side):
+            for p, hp in zip(params, host_p):
+                hp.copy_(p.detach(), non_blocking=True)
+        read_back.record(side)
 
     one()
     barrier(world)
@@ -443,6 +456,7 @@ def run_e2e(args, opt, params, grads, dev, world, total):
     e0.record(cur)
     for _ in range(args.e2e_steps):
         one()
+    cur.wait_stream(side)           # the last read-back is inside the timed region
     e1.record(cur)
     barrier(world)
     ms = max_over_ranks(e0.elapsed_time(e1), world)
