@@ -50,6 +50,54 @@ def _f32(x: float) -> float:
     return float(np.float32(x))
 
 
+def byte_range(t: torch.Tensor) -> tuple[str, int, int]:
+    """(device, first byte, end byte) of a tensor's storage, without touching
+    its values (the reference's tensor_byte_range, _moment_buffer.py:13-20)."""
+    if t.is_contiguous():
+        start = t.data_ptr()
+        return str(t.device), start, start + t.numel() * t.element_size()
+    storage = t.untyped_storage()
+    start = storage.data_ptr()
+    return str(t.device), start, start + storage.nbytes()
+
+
+def _overlapping_pairs(regions: list[tuple]) -> list[tuple[tuple, tuple]]:
+    """Pairs of overlapping (device, start, stop, owner, kind) regions, as
+    ((owner, kind), (owner, kind)); empty regions never overlap."""
+    out = []
+    active: list[tuple] = []
+    for r in sorted((r for r in regions if r[2] > r[1]), key=lambda r: (r[0], r[1])):
+        active = [a for a in active if a[0] == r[0] and a[2] > r[1]]
+        for a in active:
+            out.append(((a[3], a[4]), (r[3], r[4])))
+        active.append(r)
+    return out
+
+
+def _moment_buffers(st: dict) -> list[tuple[str, torch.Tensor]]:
+    """The writable moment tensors of one parameter's state
+    (the reference's moment_tensors, _moment_buffer.py:27-41)."""
+    out = []
+    for key in ("m1", "m2"):
+        t = st.get(key)
+        if torch.is_tensor(t) and t.numel():
+            out.append((key, t))
+        t = st.get(f"{key}_code")
+        if torch.is_tensor(t) and t.numel():
+            out.append((f"{key}_code", t))
+        qs = st.get(f"{key}_quant_state")
+        if isinstance(qs, QuantState) and torch.is_tensor(qs.absmax) and qs.absmax.numel():
+            out.append((f"{key}_absmax", qs.absmax))
+    return out
+
+
+def _set_moment_buffer(st: dict, key: str, t: torch.Tensor) -> None:
+    if key.endswith("_absmax"):
+        st[f"{key[:2]}_quant_state"].absmax = t
+    else:
+        st[key] = t
+
+
 class QuantizedAdamW(Optimizer):
     r"""AdamW with 4-bit (or FP32) moment storage, stepped on B200 by one fused kernel.
 
@@ -259,14 +307,17 @@ class QuantizedAdamW(Optimizer):
         gens[key] = gen
         return gen
 
-    def _philox_keys(self, need_m1: bool, need_m2: bool) -> tuple[int, int]:
+    def _philox_keys(self) -> tuple[int, int]:
+        """Keys of the m1 / m2 Philox streams for one step() call."""
         if self._quant_rng_seed is not None:
             return ((self._quant_rng_seed + _M1_OFFSET) % _MAX_SEED,
                     (self._quant_rng_seed + _M2_OFFSET) % _MAX_SEED)
-        # No seed: fresh keys from the global torch RNG, as the reference's
-        # unseeded SR consumes the global generator.
-        k1 = int(torch.randint(0, _MAX_SEED, (1,)).item()) if need_m1 else 0
-        k2 = int(torch.randint(0, _MAX_SEED, (1,)).item()) if need_m2 else 0
+        # No seed: one fresh key pair per step() call from the global torch
+        # RNG (the reference's unseeded SR consumes the global generator).
+        # The parameter ordinal is a Philox counter word, so the tensors of a
+        # step share the keys and stay one launch.
+        k1 = int(torch.randint(0, _MAX_SEED, (1,)).item())
+        k2 = int(torch.randint(0, _MAX_SEED, (1,)).item())
         return k1, k2
 
     # ------------------------------------------------------------ checkpoint
@@ -421,6 +472,7 @@ class _StepPlan:
         self.qgroups: dict[tuple, list] = {}
         self.fgroups: dict[tuple, list] = {}
         self.keepalive: list = []
+        self.keys: tuple[int, int] | None = None   # Philox keys of this step() call
 
     def _init_state(self, st: dict, p: torch.Tensor, m1: str, m2: str, eden: bool,
                     quantized: bool) -> None:
@@ -473,8 +525,7 @@ class _StepPlan:
                            next_bias)
         pdt, gdt = N.DTYPE_CODES[p.dtype], N.DTYPE_CODES[g.dtype]
         if not quantized:
-            self.fgroups.setdefault((p.device, pdt, gdt), []).append(
-                (p, g, st["m1"], st["m2"], hy))
+            self.fgroups.setdefault((p.device, pdt, gdt), []).append((p, g, st, hy))
             return
         m1_sr = SCHEMES[m1].round_mode != N.RTN
         m2_sr = SCHEMES[m2].round_mode != N.RTN
@@ -487,8 +538,12 @@ class _StepPlan:
         elif opt._quant_rng == "torch":
             d1, d2 = self._torch_draws(p, first, m1, m2, m1_sr, m2_sr)
             keys = (0, 0)
+        elif m1_sr or m2_sr:
+            if self.keys is None:
+                self.keys = opt._philox_keys()
+            keys = self.keys
         else:
-            keys = opt._philox_keys(m1_sr, m2_sr) if (m1_sr or m2_sr) else (0, 0)
+            keys = (0, 0)
         # legacy one-code-per-byte state is repacked before the kernel reads it
         for key in ("m1", "m2"):
             qs = st[f"{key}_quant_state"]
@@ -534,7 +589,66 @@ class _StepPlan:
         self.keepalive.extend([d1, d2])
         return d1, d2
 
+    def resolve_aliases(self) -> None:
+        """Byte-range overlap checks before the launches (the reference's GPU
+        backend refuses overlapping param/grad/moment storage,
+        _optimized.py:110-118 with _moment_buffer.py:13-41).  The fused launch
+        updates every tensor of a step at once, so the reference eager path's
+        results are kept where they can be:
+          * a gradient overlapping its own parameter is copied first (eager
+            reads the whole gradient before writing the parameter);
+          * moment buffers overlapping any other buffer are copied first
+            (eager decodes them, then stores the new moments in fresh storage,
+            which also detaches aliases across parameters after a load);
+        and a parameter overlapping another parameter or another parameter's
+        gradient is refused: eager updates them one after the other, which
+        one concurrent launch cannot reproduce."""
+        items = [(p, g, st) for its in self.qgroups.values() for p, g, st, *_ in its]
+        items += [(p, g, st) for its in self.fgroups.values() for p, g, st, *_ in its]
+        regions = []   # (device, start, stop, owner, kind)
+        moments = []
+        for k, (p, g, st) in enumerate(items):
+            regions.append((*byte_range(p), k, "param"))
+            regions.append((*byte_range(g), k, "grad"))
+            for key, t in _moment_buffers(st):
+                moments.append((k, key, t))
+                regions.append((*byte_range(t), k, key))
+        conflicts = _overlapping_pairs(regions)
+        if not conflicts:
+            return
+        copy_grad, copy_moment = set(), set()
+        for (ka, kind_a), (kb, kind_b) in conflicts:
+            kinds = {kind_a, kind_b}
+            if kinds == {"grad"}:
+                continue   # gradients are only read
+            if ka == kb and kinds == {"param", "grad"}:
+                copy_grad.add(ka)
+            elif kinds <= {"param", "grad"}:
+                raise RuntimeError(
+                    "QuantizedAdamW.step: a parameter's storage overlaps another parameter or "
+                    "its gradient; the fused step updates all tensors of a step concurrently "
+                    "and cannot reproduce one-after-the-other updates of aliased parameters")
+            else:
+                for k, kind in ((ka, kind_a), (kb, kind_b)):
+                    if kind not in ("param", "grad"):
+                        copy_moment.add((k, kind))
+        for k in copy_grad:
+            self._replace_grad(items[k][0], items[k][1])
+        for k, key, t in moments:
+            if (k, key) in copy_moment:
+                _set_moment_buffer(items[k][2], key, t.clone())
+
+    def _replace_grad(self, p, g) -> None:
+        snap = g.clone()
+        self.keepalive.append(snap)
+        for groups in (self.qgroups, self.fgroups):
+            for its in groups.values():
+                for i, it in enumerate(its):
+                    if it[0] is p:
+                        its[i] = (it[0], snap, *it[2:])
+
     def launch(self) -> None:
+        self.resolve_aliases()
         for (dev, pdt, gdt, m1, m2, eden), items in self.qgroups.items():
             hypers, hindex, tensors = [], {}, []
             for p, g, st, hy, keys, ordinal, d1, d2 in items:
@@ -563,13 +677,14 @@ class _StepPlan:
                 timing.append((ev0, ev1, sum(t.numel for t in tensors), pdt, gdt))
         for (dev, pdt, gdt), items in self.fgroups.items():
             hypers, hindex, tensors = [], {}, []
-            for p, g, m1t, m2t, hy in items:
+            for p, g, st, hy in items:
                 hk = tuple(hy.values())
                 if hk not in hindex:
                     hindex[hk] = len(hypers)
                     hypers.append(N.Hyper(hy["w1"], hy["w2"], hy["decay"], hy["neg_step"],
                                           hy["sqrt_bc2"], hy["eps"], hy["sr_bias"], hy["step"], 0, 0))
-                tensors.append(N.FTensor(N.ptr(p), N.ptr(g), N.ptr(m1t), N.ptr(m2t), p.numel(),
+                tensors.append(N.FTensor(N.ptr(p), N.ptr(g), N.ptr(st["m1"]), N.ptr(st["m2"]),
+                                         p.numel(),
                                          hindex[hk], 0))
             tarr = (N.FTensor * len(tensors))(*tensors)
             harr = (N.Hyper * len(hypers))(*hypers)

@@ -273,6 +273,33 @@ def test_one_fused_launch_per_step_for_a_many_tensor_model():
     assert opt.state[params[0]]["step"] == 2
 
 
+def test_unseeded_zipsr_steps_all_tensors_in_one_launch():
+    """Without quant_rng_seed (the reference's default) the Philox keys are
+    drawn once per step() call, not per parameter: a many-tensor ZIP-SR model
+    still takes one quantized launch per step, and re-seeding the global RNG
+    reproduces the codes."""
+    shapes = [(256, 64)] * 40 + [(4096,), (128, 128)]
+
+    def run():
+        torch.manual_seed(123)
+        params = [torch.nn.Parameter(torch.full(s, 0.01, device=DEV)) for s in shapes]
+        opt = ZIPSRAdamW4Bit(params)
+        gen = torch.Generator(device=DEV).manual_seed(5)
+        counts = []
+        for _ in range(3):
+            for p in params:
+                p.grad = torch.randn(p.shape, device=DEV, generator=gen) * 1e-3
+            before = _native.launch_count()
+            opt.step()
+            counts.append(_native.launch_count() - before)
+        return counts, torch.cat([opt.state[p]["m2_code"] for p in params])
+
+    counts, codes_a = run()
+    assert counts[1:] == [1, 1], counts          # step 1 also initialises the state
+    _, codes_b = run()
+    assert torch.equal(codes_a, codes_b)
+
+
 def test_group_hyperparameters_and_mixed_dtypes_in_one_step():
     """Two parameter groups (different lr / weight decay) and BF16 next to
     FP32 parameters: each tensor matches the oracle with its own scalars."""
@@ -306,3 +333,69 @@ def test_group_hyperparameters_and_mixed_dtypes_in_one_step():
             got = got.view(torch.int16).numpy().view(np.uint16) if p.dtype == torch.bfloat16 \
                 else got.numpy().view(np.uint32)
             np.testing.assert_array_equal(got, bits if p.dtype == torch.bfloat16 else bits.view(np.uint32))
+
+
+def test_gradient_aliasing_its_parameter_is_read_before_the_update():
+    """p.grad sharing p's storage: the step reads the whole gradient before
+    writing the parameter, as the reference's eager step does (its GPU
+    backend refuses such storage, _optimized.py:110-113)."""
+    base = (torch.randn(4096, 8, generator=torch.Generator().manual_seed(3)) * 1e-3).to(DEV)
+    a = torch.nn.Parameter(base.clone())
+    b = torch.nn.Parameter(base.clone())
+    opt_a, opt_b = ZEEDENAdamW4Bit([a]), ZEEDENAdamW4Bit([b])
+    for _ in range(2):
+        a.grad = a.detach()                 # same storage as the parameter
+        b.grad = b.detach().clone()
+        opt_a.step()
+        opt_b.step()
+    assert torch.equal(a.detach(), b.detach())
+    assert torch.equal(opt_a.state[a]["m2_code"], opt_b.state[b]["m2_code"])
+
+
+def test_overlapping_parameters_are_refused():
+    """Two parameters over overlapping bytes cannot be updated by one
+    concurrent launch the way eager updates them one after the other."""
+    storage = torch.zeros(8192 + 128, device=DEV)
+    p1 = torch.nn.Parameter(storage[:8192])
+    p2 = torch.nn.Parameter(storage[128:])
+    opt = ZEEDENAdamW4Bit([p1, p2])
+    p1.grad = torch.ones_like(p1)
+    p2.grad = torch.ones_like(p2)
+    with pytest.raises(RuntimeError, match="overlaps another parameter"):
+        opt.step()
+
+
+def test_aliased_moment_state_after_load_is_detached():
+    """A checkpoint whose two parameters share moment storage (the reference
+    marks such state, _optimized.py:53-83): each parameter decodes the shared
+    bytes, then writes its own storage, like the reference's eager step."""
+    gen = torch.Generator().manual_seed(9)
+    init = [torch.randn(64, 128, generator=gen) * 0.02 for _ in range(2)]
+    grads = [[torch.randn(64, 128, generator=gen) * 1e-3 for _ in range(2)] for _ in range(3)]
+
+    def run(alias):
+        ps = [torch.nn.Parameter(x.clone().to(DEV)) for x in init]
+        opt = ZEEDENAdamW4Bit(ps)
+        for p, g in zip(ps, grads[0]):
+            p.grad = g.to(DEV)
+        opt.step()
+        src = opt.state[ps[0]]
+        for key in ("m1_code", "m2_code"):
+            opt.state[ps[1]][key] = src[key] if alias else src[key].clone()
+        for key in ("m1_quant_state", "m2_quant_state"):
+            qs = copy.copy(src[key])
+            qs.absmax = src[key].absmax if alias else src[key].absmax.clone()
+            opt.state[ps[1]][key] = qs
+        for t in (1, 2):
+            for p, g in zip(ps, grads[t]):
+                p.grad = g.to(DEV)
+            opt.step()
+        return ps, opt
+
+    ps_a, opt_a = run(alias=True)
+    ps_b, opt_b = run(alias=False)
+    assert opt_a.state[ps_a[0]]["m1_code"].data_ptr() != opt_a.state[ps_a[1]]["m1_code"].data_ptr()
+    for pa, pb in zip(ps_a, ps_b):
+        assert torch.equal(pa.detach(), pb.detach())
+        for key in ("m1_code", "m2_code"):
+            assert torch.equal(opt_a.state[pa][key], opt_b.state[pb][key])

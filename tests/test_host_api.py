@@ -15,7 +15,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from adamw4bit_b200 import AdamW8bit, QuantizedAdamW, ZEEDENAdamW4Bit, ZIPSRAdamW4Bit
-from adamw4bit_b200.optimizer import hyper_scalars
+from adamw4bit_b200.optimizer import _overlapping_pairs, byte_range, hyper_scalars
 from adamw4bit_b200.quantization import QuantState, default_block_size, is_4bit_scheme
 from adamw4bit_b200.zero import ShardPlan, grad_layout
 
@@ -89,6 +89,28 @@ def test_step_on_cpu_tensors_fails_loudly():
     p.grad = torch.ones_like(p)
     with pytest.raises(RuntimeError, match="CUDA devices only"):
         opt.step()
+
+
+def test_byte_range_overlap_sweep():
+    """Overlap detection of the pre-launch alias checks (the reference's
+    tensor_byte_range / overlaps, _moment_buffer.py:13-24): views of one
+    buffer overlap exactly when their byte ranges intersect, non-contiguous
+    views count their whole storage, and empty tensors never overlap."""
+    base = torch.zeros(1024)
+    a, b, c = base[0:512], base[511:600], base[600:700]
+    other = torch.zeros(64)
+    whole = torch.zeros(64, 4)
+    strided = whole[:, 1]
+    regions = [(*byte_range(a), 0, "param"), (*byte_range(b), 1, "param"),
+               (*byte_range(c), 2, "grad"), (*byte_range(other), 3, "m1_code"),
+               (*byte_range(torch.zeros(0)), 4, "m2_code")]
+    pairs = {frozenset(p) for p in _overlapping_pairs(regions)}
+    assert pairs == {frozenset({(0, "param"), (1, "param")})}
+    d, s0, e0 = byte_range(strided)
+    assert e0 - s0 == 64 * 4 * 4   # the whole storage
+    regions += [(d, s0, e0, 5, "m2_absmax"), (*byte_range(whole[0, :1]), 6, "param")]
+    pairs = {frozenset(p) for p in _overlapping_pairs(regions)}
+    assert frozenset({(5, "m2_absmax"), (6, "param")}) in pairs
 
 
 def test_eligibility_mirrors_torchao_rule():
