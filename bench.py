@@ -3,26 +3,38 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     torchrun --nproc-per-node N bench.py --gpus N ...          (N > 1)
 
-Workload: the Llama-3-8B parameter set (vocab 128256, d 4096, 32 layers, ffn
-14336, 32/8 heads, untied head: 291 tensors, 8.03 B values, all quantized),
-FP32 master parameters, BF16 gradients N(0, 1e-4), ZEEDENAdamW4Bit (NF4 m1 +
-zero-exclusive Dyn4 m2 with EDEN).  N=1 steps the whole set through the public
-optimizer API; N>1 shards it ZeRO-1 style (ZeRO1AdamW4Bit): FP32 master
-weights sharded over the ranks, a BF16 model copy written by the update kernel
-and all-gathered with NCCL (``--gather fp32`` gathers FP32 parameters instead).
+Workload (``value``, every N): the Llama-3-8B parameter set (vocab 128256,
+d 4096, 32 layers, ffn 14336, 32/8 heads, untied head: 291 tensors, 8.03 B
+values, all quantized), FP32 master weights, BF16 gradients N(0, 1e-4),
+ZE-EDEN (NF4 m1 + zero-exclusive Dyn4 m2 with EDEN), stepped by
+ZeRO1AdamW4Bit: the update kernel updates the FP32 masters and writes the BF16
+model copy the next forward pass reads.  At N=1 one GPU owns every value; at
+N>1 the masters and moments are sharded ZeRO-1 style and the BF16 model is
+all-gathered (NCCL, or the kernel's own NVSwitch multicast stores with
+``--gather multicast``), so every N does the same work per step.
 Synthetic data, random-init weights.
 
 A step is one pass of the optimizer over every parameter.  ``value`` is the
-whole-job elements/s with everything resident in HBM (the 56 GB working set
-is far larger than L2, so no flush is needed between steps); ``e2e`` is the
-same metric through the public API with the gradients copied in from pinned
-host memory and the updated parameters copied back each step.
-``--impl reference`` times the CPU oracle port of the reference algorithm on
-the host's cores on a bounded sample of the same workload.  ``--impl
-reference-gpu`` / ``reference-gpu-eager`` / ``reference-cpu`` /
-``reference-cpu-eager`` time the reference's own implementation (from the
-offline install under baseline/_ref) on the GPU or on the host cores, for
-comparison only.
+whole-job elements/s with everything resident in HBM (the working set is far
+larger than the 126 MB L2, so no flush is needed between steps); ``e2e`` is
+the same metric with each rank's gradients copied in from pinned host memory
+and its updated BF16 model shard copied back every step.
+
+N=1 also reports, as extra keys:
+  * ``drop_in``: the reference's own API, ZEEDENAdamW4Bit with FP32
+    parameters and BF16 gradients (no model copy), on the same parameter set;
+  * ``zip_sr``: ZIPSRAdamW4Bit on BASELINE configuration 4's Llama-1B set,
+    BF16 parameters and gradients, and FP32 parameters with BF16 gradients;
+  * ``cpu_baseline``: the C/OpenMP port of the reference algorithm on a
+    2^27-value sample, and the reference's own CPU step (from the offline
+    install under baseline/_ref), eager (optimized=False) and chunked
+    (optimized=True), on one 4096x4096 FP32 tensor, all host threads.
+
+``--impl reference`` times the CPU port of the reference algorithm on the
+host's cores on a bounded sample of the same workload (the reference itself
+is Python on PyTorch).  ``--impl reference-gpu`` / ``reference-gpu-eager`` /
+``reference-cpu`` / ``reference-cpu-eager`` time the reference's own
+implementation on the GPU or on the host cores, for comparison only.
 """
 
 from __future__ import annotations
@@ -43,12 +55,33 @@ if ROOT not in sys.path:
 
 METRIC = "optimizer-step elements/s"
 UNIT = "elements/s"
-B_PER_ELEM = 4 + 4 + 2 + 1 + 1 + 2 * 8 / 128   # FP32 p r+w, BF16 g r, codes r+w, scales r+w
-WORKLOAD = "llama3-8b ZE-EDEN fp32-master/bf16-grad (BASELINE config 5)"
+B_STATE = 2 * (0.5 + 0.5) + 2 * 2 * 4 / 128   # m1/m2 packed codes and block scales, read + write
+WORKLOAD = ("llama3-8b ZE-EDEN: FP32 master weights + BF16 model copy, BF16 grads "
+            "(BASELINE config 5)")
+
+
+def bytes_per_value(p_bytes: int, g_bytes: int, model_copy: bool) -> float:
+    """Algorithmic HBM bytes of one value's step: parameter read + write,
+    gradient read, moment state, and the BF16 model-copy write."""
+    return 2 * p_bytes + g_bytes + B_STATE + (2 if model_copy else 0)
+
+
+B_PER_ELEM = bytes_per_value(4, 2, True)   # the config-5 workload: 14.125 B/value
 
 
 def llama3_8b_shapes() -> list[tuple[int, ...]]:
     V, d, L, ffn, kv = 128256, 4096, 32, 14336, 1024
+    shapes = [(V, d)]
+    for _ in range(L):
+        shapes += [(d, d), (kv, d), (kv, d), (d, d), (ffn, d), (ffn, d), (d, ffn), (d,), (d,)]
+    shapes += [(d,), (V, d)]
+    return shapes
+
+
+def llama_1b_shapes() -> list[tuple[int, ...]]:
+    """vocab 32000, d 2048, 16 layers, ffn 5632,
+    32/8 heads (kv dim 512), untied head: 147 tensors, 852.6 M values."""
+    V, d, L, ffn, kv = 32000, 2048, 16, 5632, 512
     shapes = [(V, d)]
     for _ in range(L):
         shapes += [(d, d), (kv, d), (kv, d), (d, d), (ffn, d), (ffn, d), (d, ffn), (d,), (d,)]
@@ -206,7 +239,10 @@ def run_reference(args, rank, world):
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": WORKLOAD, "sample_values": sample, "l2": "inputs > L2"},
             "impl": "reference",
-            "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+            "cpu_baseline": {**{k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+                             **{k: ({kk: vv for kk, vv in v.items() if kk != "seconds_per_step"}
+                                    if isinstance(v, dict) else v)
+                                for k, v in reference_cpu_rates(max(1, min(args.steps, 3))).items()}},
             "e2e": {"value": base["value"], "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
@@ -286,8 +322,109 @@ def run_reference_torch(args, rank, device: str, eager: bool):
                       "warmup_seconds": warm_s, **extra}), flush=True)
 
 
+def reference_cpu_rates(steps: int) -> dict:
+    """The reference's own ZEEDENAdamW4Bit.step on the host cores (all
+    threads), eager (optimized=False, adamw.py:472-805) and chunked
+    (optimized=True, _optimized.py:145-247), on one 4096x4096 FP32 tensor
+    with BF16 gradients: median wall time of `steps` steps after one warm-up
+    step.  Imported from the offline install under baseline/_ref."""
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    if not os.path.isdir(os.path.join(ref, "adamw4bit")):
+        return {"unavailable": "baseline/_ref is not installed"}
+    if ref not in sys.path:
+        sys.path.insert(0, ref)
+    from adamw4bit import ZEEDENAdamW4Bit as RefZE
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    gen = torch.Generator().manual_seed(0)
+    init = torch.randn(4096, 4096, generator=gen) * 0.02
+    grad = (torch.randn(4096, 4096, generator=gen) * 1e-4).to(torch.bfloat16)
+    out = {}
+    for key, optimized in (("reference_eager", False), ("reference_optimized", True)):
+        p = torch.nn.Parameter(init.clone())
+        p.grad_dtype = None   # FP32 parameter, BF16 gradient
+        opt = RefZE([p], lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1,
+                    optimized=optimized)
+        p.grad = grad
+        opt.step()
+        times = []
+        for _ in range(steps):
+            t0 = time.perf_counter()
+            opt.step()
+            times.append(time.perf_counter() - t0)
+        med = statistics.median(times)
+        out[key] = {"value": p.numel() / med, "unit": UNIT, "cores": threads,
+                    "kind": "reference",
+                    "sample": f"4096x4096 FP32 param, BF16 grads, ZEEDENAdamW4Bit "
+                              f"optimized={optimized}, median of {steps} steps after 1 "
+                              "warm-up step (baseline/_ref, CPU)",
+                    "seconds_per_step": med}
+    return out
+
+
+def timed_steps(opt, steps: int, warmup: int) -> tuple[float, float, float]:
+    """Runs warm-up then `steps` optimizer steps; returns (device ms per step,
+    fused-kernel ms per step, values updated per step)."""
+    for _ in range(warmup):
+        opt.step()
+    torch.cuda.synchronize()
+    opt.launch_timings = []
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        opt.step()
+    e1.record()
+    torch.cuda.synchronize()
+    t = opt.launch_timings
+    opt.launch_timings = None
+    kms = sum(a.elapsed_time(b) for a, b, *_ in t) / steps
+    vals = sum(x[2] for x in t) / steps
+    return e0.elapsed_time(e1) / steps, kms, vals
+
+
+def leg_record(kernel_ms: float, values: float, bpv: float, peak: float, step_ms: float) -> dict:
+    gbs = values * bpv / (kernel_ms / 1e3) / 1e9
+    return {"values": int(values), "step_ms": round(step_ms, 4), "launch_ms": round(kernel_ms, 4),
+            "elements_per_s": values / (kernel_ms / 1e3), "bytes_per_value": bpv,
+            "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak, 4)}
+
+
+def run_legs(args, dev, peak: float) -> dict:
+    """N=1 extra keys: the drop-in API on config 5 and the ZIP-SR legs."""
+    from adamw4bit_b200 import ZEEDENAdamW4Bit, ZIPSRAdamW4Bit
+
+    out = {}
+    params, grads = make_workload(dev, llama3_8b_shapes(), param_dtype=torch.float32)
+    for p, g in zip(params, grads):
+        p.grad = g
+    opt = ZEEDENAdamW4Bit(params, lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    step_ms, kms, vals = timed_steps(opt, args.steps, args.warmup)
+    out["drop_in"] = {"api": "ZEEDENAdamW4Bit", "workload": "llama3-8b, FP32 params updated in "
+                      "place, BF16 grads (BASELINE config 5 through the reference's API)",
+                      **leg_record(kms, vals, bytes_per_value(4, 2, False), peak, step_ms)}
+    del opt, params, grads
+    torch.cuda.empty_cache()
+    zs = {"api": "ZIPSRAdamW4Bit", "workload": "llama-1b (BASELINE config 4 parameter set), "
+          "quant_rng_seed=1234, in-kernel Philox draws"}
+    for key, pdt in (("bf16_params_bf16_grads", torch.bfloat16),
+                     ("fp32_params_bf16_grads", torch.float32)):
+        params, grads = make_workload(dev, llama_1b_shapes(), param_dtype=pdt)
+        for p, g in zip(params, grads):
+            p.grad = g
+        opt = ZIPSRAdamW4Bit(params, lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1,
+                             quant_rng_seed=1234)
+        step_ms, kms, vals = timed_steps(opt, args.steps, args.warmup)
+        zs[key] = leg_record(kms, vals, bytes_per_value(pdt.itemsize, 2, False), peak, step_ms)
+        del opt, params, grads
+        torch.cuda.empty_cache()
+    out["zip_sr"] = zs
+    return out
+
+
 def run_ours(args, rank, world, local):
-    from adamw4bit_b200 import ZEEDENAdamW4Bit, ZIPSRAdamW4Bit, _native
+    from adamw4bit_b200 import _native
     from adamw4bit_b200.zero import ZeRO1AdamW4Bit
 
     dev = torch.device("cuda", local)
@@ -298,25 +435,18 @@ def run_ours(args, rank, world, local):
     if args.values:
         shapes = [(args.values,)]   # single-tensor case (profiling)
     total = sum(int(torch.Size(s).numel()) for s in shapes)
-    master = world > 1 and args.gather in ("bf16", "multicast")
+    master = args.gather != "fp32"
     params, grads = make_workload(dev, shapes,
                                   param_dtype=torch.bfloat16 if master else torch.float32)
-    if world == 1:
-        cls = ZEEDENAdamW4Bit if args.recipe == "ze-eden" else ZIPSRAdamW4Bit
-        opt = cls(params, lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1,
-                  quant_rng_seed=None if args.recipe == "ze-eden" else 1234)
-        step_fn = opt.step
-        updated_per_rank = total
-    else:
-        # FP32 masters sharded over the ranks; with --gather bf16 the model is
-        # BF16 (written by the update kernel) and the all-gather moves 2 B/value
-        opt = ZeRO1AdamW4Bit(params, recipe=args.recipe, rounds=args.rounds,
-                             master_weights=master, reserve_sms=args.reserve_sms,
-                             gather="multicast" if args.gather == "multicast" else "nccl",
-                             grad_reduce=args.grad_reduce)
-        step_fn = opt.step
-        updated_per_rank = opt.owned_numel()
-    b_per_elem = B_PER_ELEM + (2 if master else 0)   # + the BF16 model copy write
+    # FP32 masters (sharded over the ranks at N>1) and the BF16 model copy
+    # written by the update kernel; at N>1 the model is all-gathered
+    opt = ZeRO1AdamW4Bit(params, recipe=args.recipe, rounds=args.rounds if world > 1 else 1,
+                         master_weights=master, reserve_sms=args.reserve_sms,
+                         gather="multicast" if args.gather == "multicast" else "nccl",
+                         grad_reduce=args.grad_reduce, quant_rng_seed=1234)
+    step_fn = opt.step
+    updated_per_rank = opt.owned_numel()
+    b_per_elem = bytes_per_value(4, 2, master)
     zero2 = world > 1 and args.grad_reduce == "multicast"
     for p, g in zip(params, grads):
         if zero2:   # this rank's unreduced gradients, in the bound symmetric buffer
@@ -328,8 +458,7 @@ def run_ours(args, rank, world, local):
     barrier(world)
 
     sampler = ClockSampler(torch.cuda.current_device() if world == 1 else local)
-    if rank == 0 or world > 1:
-        sampler.start()
+    sampler.start()
     opt.launch_timings = []
     launches0 = _native.launch_count()
     barrier(world)
@@ -363,20 +492,21 @@ def run_ours(args, rank, world, local):
     achieved = per_launch_elems * b_per_elem / (per_launch_ms / 1e3) / 1e9
     tr = traffic_record()
     traffic = None
-    if tr and tr.get("bytes_per_value") and not master:   # captured on the N=1 workload
+    if tr and tr.get("bytes_per_value") and tr.get("bytes_per_value_algorithmic") == b_per_elem:
         traffic = tr["bytes_per_value"] * per_launch_elems
+    kname = "aw4::step_kernel<F32,BF16,RTN,%s> (fused decode+AdamW+encode+BF16 model copy)" % (
+        "RTN" if args.recipe == "ze-eden" else "SR_UPDATE")
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm_peak, "unit": "GB/s",
                 "frac": round(achieved / hbm_peak, 4), "traffic": traffic,
-                "peak_source": peak_src,
-                "algorithmic_bytes_per_value": b_per_elem,
-                "kernel": "aw4::step_kernel<F32,BF16,RTN,%s> (fused decode+AdamW+encode)"
-                          % ("RTN" if args.recipe == "ze-eden" else "SR_UPDATE"),
-                "launch_ms": round(per_launch_ms, 4), "values_per_launch": int(per_launch_elems)}
+                "peak_source": peak_src, "algorithmic_bytes_per_value": b_per_elem,
+                "kernel": kname, "launch_ms": round(per_launch_ms, 4),
+                "values_per_launch": int(per_launch_elems)}
 
-    e2e = None
-    if args.e2e_steps > 0:
-        e2e = (run_e2e(args, opt, params, grads, dev, world, total) if world == 1
-               else run_e2e_sharded(args, opt, params, grads, dev, world, total))
+    e2e = run_e2e(args, opt, dev, world, total) if args.e2e_steps > 0 else None
+    gather_mode = opt.gather_mode
+    del opt, params, grads
+    torch.cuda.empty_cache()
+    legs = run_legs(args, dev, hbm_peak) if (world == 1 and args.legs) else {}
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
@@ -391,11 +521,11 @@ def run_ours(args, rank, world, local):
                            "parallelism": "single GPU" if world == 1 else
                            f"{'zero2' if zero2 else 'zero1'}-dp{world}, "
                            f"{'bf16 model' if master else 'fp32'} gather "
-                           f"({getattr(opt, 'gather_mode', 'nccl')})"
+                           f"({gather_mode})"
                            + (", gradient reduce-scatter fused into the update "
                               "(multimem.ld_reduce)" if zero2 else
                               ", gradients already reduced"),
-                           "l2": "no flush: 56 GB working set >> 126 MB L2"},
+                           "l2": "no flush: 72 GB working set >> 126 MB L2"},
                 "roofline": roofline,
                 "update_only": {"values_per_rank": updated_per_rank,
                                 "kernel_ms_per_step_max_rank": kernel_ms_max / args.steps,
@@ -403,6 +533,14 @@ def run_ours(args, rank, world, local):
                                     updated_per_rank * args.steps / (kernel_ms_max / 1e3)},
                 "clocks": clocks, "gpu_launches": int(launches),
                 "e2e": e2e}
+        if world > 1:
+            # every GPU receives the whole model minus its own shard each step
+            nv = (world - 1) / world * total * (2 if master else 4)
+            line["gather"] = {"ingress_bytes_per_gpu": nv,
+                              "ingress_gbs": round(nv / (ms_per_step / 1e3) / 1e9, 1),
+                              "peak_gbs": 770.0,
+                              "peak_source": "measured peer copy, per direction",
+                              "floor_ms": round(nv / 770e9 * 1e3, 2)}
         if zero2:
             # per GPU and step, each NVLink direction carries 2 B per value:
             # out, its gradients to the switch's reductions of every shard
@@ -414,42 +552,60 @@ def run_ours(args, rank, world, local):
                               "achieved_gbs": round(nv / (ms_per_step / 1e3) / 1e9, 1),
                               "peak_gbs": 770.0, "peak_source": "measured peer copy, per direction",
                               "frac": round(nv / (ms_per_step / 1e3) / 1e9 / 770.0, 4)}
+        line.update(legs)
         if world == 1 and args.cpu_sample > 0:
-            line["cpu_baseline"] = {k: v for k, v in cpu_oracle_rate(
+            cb = {k: v for k, v in cpu_oracle_rate(
                 args.cpu_sample, args.cpu_steps).items() if k != "seconds_per_step"}
+            for k, v in reference_cpu_rates(args.cpu_steps).items():
+                cb[k] = {kk: vv for kk, vv in v.items() if kk != "seconds_per_step"} \
+                    if isinstance(v, dict) else v
+            line["cpu_baseline"] = cb
         print(json.dumps(line), flush=True)
 
 
-def run_e2e(args, opt, params, grads, dev, world, total):
-    """Public-API step with host buffers: pinned grads -> device, step,
-    updated params -> pinned host, all inside the timed region.  The
-    read-back of step t's parameters runs on a second stream and overlaps the
-    upload of step t+1's gradients (PCIe carries both directions at once);
-    step t+1's update waits for that read-back before it overwrites the
-    parameters, and the timed region ends after the last read-back."""
-    host_g = [g.detach().to("cpu").pin_memory() for g in grads]
-    host_p = [torch.empty(p.shape, dtype=p.dtype, pin_memory=True) for p in params]
-    h2d = sum(g.numel() * g.element_size() for g in host_g)
-    d2h = sum(p.numel() * p.element_size() for p in host_p)
+def run_e2e(args, opt, dev, world, total):
+    """End to end through the optimizer with host buffers: each rank copies in
+    its gradients from pinned host memory (its owned segments; with the
+    ZeRO-2 reduction, its full local gradients), steps, and copies its updated
+    BF16 model shard back to pinned host memory, all inside the timed region.
+    The read-back of step t runs on a second stream and overlaps the upload of
+    step t+1's gradients (PCIe carries both directions at once); step t+1's
+    update waits for that read-back before it overwrites the model, and the
+    timed region ends after the last read-back.  Afterwards a strided sample
+    of the host copy is compared with the device model."""
+    segs = [seg for round_segs in opt.segments for seg in round_segs]
+    if opt.grad_reduce == "multicast":
+        segs = [(ti, 0, p.numel(), 0) for ti, p in enumerate(opt.params)]
+    host_g = [opt.params[ti].grad.reshape(-1)[s:s + n].to("cpu").pin_memory()
+              for ti, s, n, _ in segs]
+    small = [opt.all_params[i] for i in opt.sindex]
+    host_gs = [p.grad.to("cpu").pin_memory() for p in small]
+    owned = [(a, b) for a, b in opt.owned if b > a]
+    host_p = [torch.empty(b - a, dtype=opt.flat.dtype, pin_memory=True) for a, b in owned]
+    h2d = sum(h.numel() * h.element_size() for h in host_g + host_gs)
+    d2h = sum(h.numel() * h.element_size() for h in host_p)
     cur = torch.cuda.current_stream(dev)
     side = torch.cuda.Stream(dev)
     read_back = torch.cuda.Event()
     read_back.record(side)          # created and complete: nothing to wait for yet
 
     def one():
-        for p, hg in zip(params, host_g):
+        for (ti, s, n, _), hg in zip(segs, host_g):
+            opt.params[ti].grad.reshape(-1)[s:s + n].copy_(hg, non_blocking=True)
+        for p, hg in zip(small, host_gs):
             p.grad.copy_(hg, non_blocking=True)
-        cur.wait_event(read_back)   # the previous step's parameters are on the host
+        cur.wait_event(read_back)   # the previous step's model is on the host
         opt.step()
         stepped = torch.cuda.Event()
         stepped.record(cur)
         side.wait_event(stepped)
         with torch.cuda.stream(side):
-            for p, hp in zip(params, host_p):
-                hp.copy_(p.detach(), non_blocking=True)
+            for (a, b), hp in zip(owned, host_p):
+                hp.copy_(opt.flat[a:b], non_blocking=True)
         read_back.record(side)
 
     one()
+    cur.wait_stream(side)           # the timed region starts with an idle side stream
     barrier(world)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
@@ -460,47 +616,16 @@ def run_e2e(args, opt, params, grads, dev, world, total):
     e1.record(cur)
     barrier(world)
     ms = max_over_ranks(e0.elapsed_time(e1), world)
-    del host_g, host_p
+    torch.cuda.synchronize()
+    for (a, b), hp in zip(owned, host_p):
+        stride = max(1, (b - a) // 4099)
+        if not torch.equal(hp[::stride].to(dev), opt.flat[a:b][::stride]):
+            raise RuntimeError("e2e: the host copy does not hold the stepped model")
+    del host_g, host_gs, host_p
     return {"value": total * args.e2e_steps / (ms / 1e3), "unit": UNIT,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "ms_per_step": ms / args.e2e_steps, "steps": args.e2e_steps}
-
-
-def run_e2e_sharded(args, opt, params, grads, dev, world, total):
-    """ZeRO-1 end to end: each rank copies in the gradient values it owns from
-    pinned host memory, steps (update + NCCL all-gather), and copies its
-    updated parameter shard back to pinned host memory."""
-    segs = [seg for round_segs in opt.segments for seg in round_segs]
-    if opt.grad_reduce == "multicast":   # ZeRO-2: every rank brings its full local gradients
-        segs = [(ti, 0, p.numel(), 0) for ti, p in enumerate(params)]
-    host_g = [grads[ti].reshape(-1)[s:s + n].to("cpu").pin_memory() for ti, s, n, _ in segs]
-    owned = [(a, b) for a, b in opt.owned if b > a]
-    host_p = [torch.empty(b - a, dtype=opt.flat.dtype, pin_memory=True) for a, b in owned]
-    h2d = sum(h.numel() * h.element_size() for h in host_g)
-    d2h = sum(h.numel() * h.element_size() for h in host_p)
-    cur = torch.cuda.current_stream(dev)
-
-    def one():
-        for (ti, s, n, _), hg in zip(segs, host_g):
-            params[ti].grad.reshape(-1)[s:s + n].copy_(hg, non_blocking=True)
-        opt.step()
-        for (a, b), hp in zip(owned, host_p):
-            hp.copy_(opt.flat[a:b], non_blocking=True)
-
-    one()
-    barrier(world)
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    e0.record(cur)
-    for _ in range(args.e2e_steps):
-        one()
-    e1.record(cur)
-    barrier(world)
-    ms = max_over_ranks(e0.elapsed_time(e1), world)
-    return {"value": total * args.e2e_steps / (ms / 1e3), "unit": UNIT,
-            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "bytes_are_per_rank": True, "ms_per_step": ms / args.e2e_steps,
-            "steps": args.e2e_steps}
+            "bytes_are_per_rank": world > 1, "ms_per_step": ms / args.e2e_steps,
+            "steps": args.e2e_steps, "readback_checked": True}
 
 
 def main():
@@ -524,7 +649,9 @@ def main():
                          "replica by the update kernel through NVSwitch multicast, or "
                          "all-gathered by NCCL (bf16, default), or the FP32 parameters "
                          "all-gathered by NCCL")
-    ap.add_argument("--e2e-steps", type=int, default=2)
+    ap.add_argument("--e2e-steps", type=int, default=4)
+    ap.add_argument("--no-legs", dest="legs", action="store_false",
+                    help="N=1: skip the drop-in and ZIP-SR legs")
     ap.add_argument("--cpu-sample", type=int, default=1 << 27,
                     help="values in the CPU-oracle sample (0: skip)")
     ap.add_argument("--cpu-steps", type=int, default=3)
