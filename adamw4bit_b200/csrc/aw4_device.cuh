@@ -547,6 +547,34 @@ __device__ __forceinline__ void lut_search8(const SchemeRegs& r, const float x[8
     for (int i = 0; i < 8; i += 2) lut_search2(r, x[i], x[i + 1], code + i);
 }
 
+
+// lut_search8 for an RTN scheme, returning the 8 codes packed as nibbles
+// (value i in bits 4i..4i+3): code = count - ge (ge = -1 when x >= next) is
+// accumulated as count * 16^i + ge * -16^i with integer multiply-adds.
+__device__ __forceinline__ uint32_t lut_pack8(const SchemeRegs& r, const float x[8]) {
+    uint32_t packed = 0;
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) {
+        f2 t;
+        asm("fma.rz.f32x2 %0, %1, %2, %3;" : "=l"(t)
+            : "l"(pk2(x[i], x[i + 1])), "l"(pk2(r.half, r.half)), "l"(pk2(r.bias, r.bias)));
+        float b0, b1;
+        upk2(t, b0, b1);
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+            const uint32_t addr = __float_as_uint(k ? b1 : b0) * 8u + r.tab_biased;
+            float next;
+            int count, ge;
+            asm("ld.shared.v2.b32 {%0, %1}, [%2];" : "=f"(next), "=r"(count) : "r"(addr));
+            asm("set.ge.s32.f32 %0, %1, %2;" : "=r"(ge) : "f"(k ? x[i + 1] : x[i]), "f"(next));
+            const uint32_t m = 1u << (4 * (i + k));
+            asm("mad.lo.u32 %0, %1, %2, %0;" : "+r"(packed) : "r"(count), "r"(m));
+            asm("mad.lo.u32 %0, %1, %2, %0;" : "+r"(packed) : "r"(ge), "r"(0u - m));
+        }
+    }
+    return packed;
+}
+
 // Level of a code from the codebook held in registers: lane l keeps
 // cbv = cb[l % 16], and a shuffle reads lane `code`.
 __device__ __forceinline__ float level_of(float cbv, int code) {
@@ -570,6 +598,16 @@ __device__ __forceinline__ void decode8(float cbv, uint32_t w, float scale, floa
         asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(pk2(lv[i], lv[i + 1])), "l"(ss), "l"(zz));
         upk2(r, v[i], v[i + 1]);
     }
+}
+
+// Decodes 8 packed codes from the block's scaled codebook: lane 16h + k of
+// the block's 16-lane group holds cbs = RN(cb[k] * scale), and a shuffle
+// confined to the group reads lane `code` (the segment keeps only the low 4
+// bits of the index, so w >> 4i needs no mask).  RN(cb[k] * scale) is the
+// product decode8 forms.
+__device__ __forceinline__ void decode8s(float cbs, uint32_t w, float v[8]) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = __shfl_sync(0xffffffffu, cbs, (int)(w >> (4 * i)), 16);
 }
 
 // torch.searchsorted(cb, x) (left): the ATen lower-bound loop, NaN -> 16.

@@ -364,6 +364,7 @@ __device__ __forceinline__ uint32_t encode_fast_codes(const SmemScheme& S, const
     float x[8];
     int code[8];
     vdiv_markstein8(x, v, sc, rcp_nr(sc));
+    if (MODE == AW4_RTN && !eden) return lut_pack8(R, x);
     int idxs[8];
     lut_search8(R, x, idxs);
 #pragma unroll
