@@ -18,10 +18,10 @@ LIB_PATH = os.path.join(HERE, "libadamw4bit_b200.so")
 
 AW4_OK, AW4_ERR_INVALID, AW4_ERR_CUDA, AW4_ERR_UNSUPPORTED = 0, 1, 2, 3
 F32, BF16, F16 = 0, 1, 2
-RTN, SR_VALUE, SR_UPDATE = 0, 1, 2
+RTN, SR_VALUE, SR_UPDATE, FP32_MOMENT = 0, 1, 2, 3
 BLOCK = 128
 LUT_BINS = 1024
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 DTYPE_CODES = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}
 

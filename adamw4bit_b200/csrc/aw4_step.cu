@@ -200,9 +200,11 @@ __device__ __forceinline__ void load_uniforms(float u[8], const float* draws,
 template <int PT, int GT, int M1, int M2, bool GMC>
 __global__ void __launch_bounds__(kThreads, 4)
 step_kernel(const __grid_constant__ StepLaunch L) {
+    // F1: m1 is kept as float32 values (c1 holds them; no codes, no scales)
+    constexpr bool F1 = M1 == AW4_FP32_MOMENT;
     __shared__ __align__(16) StepSmem sm;
     const int tid = threadIdx.x;
-    load_scheme(sm.s1, L.m1, tid, kThreads);
+    if (!F1) load_scheme(sm.s1, L.m1, tid, kThreads);
     load_scheme(sm.s2, L.m2, tid, kThreads);
     __syncthreads();
 
@@ -239,19 +241,23 @@ step_kernel(const __grid_constant__ StepLaunch L) {
                 } else {
                     Elem<GT>::load8(D.grad, e0, gr);
                 }
-                w1 = __ldcs(reinterpret_cast<const unsigned int*>(D.c1 + (e0 >> 1)));
+                if constexpr (F1) {
+                    Elem<AW4_F32>::load8(D.c1, e0, m1);
+                } else {
+                    w1 = __ldcs(reinterpret_cast<const unsigned int*>(D.c1 + (e0 >> 1)));
+                    s1 = __ldcs(D.s1 + blk);
+                }
                 w2 = __ldcs(reinterpret_cast<const unsigned int*>(D.c2 + (e0 >> 1)));
-                s1 = __ldcs(D.s1 + blk);
                 s2 = __ldcs(D.s2 + blk);
             } else {
 #pragma unroll
-                for (int i = 0; i < 8; ++i) p[i] = gr[i] = 0.0f;
+                for (int i = 0; i < 8; ++i) p[i] = gr[i] = m1[i] = 0.0f;
             }
             // Packed f32x2 arithmetic throughout: multiplies, FMAs, and
             // additions as fma(a, one, b) (no multiply can be fused into them).
             // decode (quantization.py:996-999)
             float d[8], q[8];
-            decode8s(fmul(r1.cbv, s1), w1, m1);
+            if (!F1) decode8s(fmul(r1.cbv, s1), w1, m1);
             decode8s(fmul(r2.cbv, s2), w2, m2);
             vfmas8(d, -one, m1, gr);                 // g - m1
             vfmas8(m1, H.w1, d, m1);                 // m1.lerp_(g, 1-b1)  (adamw.py:557)
@@ -268,10 +274,10 @@ step_kernel(const __grid_constant__ StepLaunch L) {
             const float gmax2 = group_max16(amax2);
             const float sc2 = max_nan(gmax2, kScaleFloor);
             bool ok = active && amax1 <= H.m1_fast_max && amax2 <= H.m2_fast_max &&
-                      sc1 <= kMarksteinMaxDivisor && sc2 <= kMarksteinMaxDivisor &&
+                      (F1 || sc1 <= kMarksteinMaxDivisor) && sc2 <= kMarksteinMaxDivisor &&
                       (gmax2 >= kScaleFloor || !L.eden);
             ok = none_tiny_warp(nt, ok);
-            if (M1 != AW4_RTN) ok = none_tiny_warp(m1, ok);
+            if (M1 == AW4_SR_VALUE) ok = none_tiny_warp(m1, ok);
             if (M2 != AW4_RTN || L.eden) ok = none_tiny_warp(m2, ok);
             float u[8];
             if (__all_sync(0xffffffffu, ok)) {
@@ -282,16 +288,20 @@ step_kernel(const __grid_constant__ StepLaunch L) {
                 vadd8(p, q, p, one);                 // p.addcdiv_(m1, den, -lr/bc1)
                 Elem<PT>::store8(D.param, e0, p);
                 if (D.pc != nullptr) store_model_copy(D, e0, p);
-                if (M1 != AW4_RTN) load_uniforms<M1>(u, D.d1, H.m1_key, H, D, e0, true);
-                float ns1, ns2;
-                const uint32_t c1 =
-                    encode_fast<M1>(sm.s1, r1, g, m1, sc1, u, 0, 0, H.sr_bias, H.eps, H.sr_rbias,
-                                    one, &ns1);
+                float ns1 = 0.0f, ns2;
+                uint32_t c1 = 0;
+                if constexpr (F1) {
+                    Elem<AW4_F32>::store8(D.c1, e0, m1);   // the FP32 moment itself
+                } else {
+                    if (M1 == AW4_SR_VALUE) load_uniforms<M1>(u, D.d1, H.m1_key, H, D, e0, true);
+                    c1 = encode_fast<M1>(sm.s1, r1, g, m1, sc1, u, 0, 0, H.sr_bias, H.eps,
+                                         H.sr_rbias, one, &ns1);
+                }
                 if (M2 != AW4_RTN) load_uniforms<M2>(u, D.d2, H.m2_key, H, D, e0, true);
                 const uint32_t c2 =
                     encode_fast<M2>(sm.s2, r2, g, m2, sc2, u, zf2, L.eden, H.sr_bias, H.eps,
                                     H.sr_rbias, one, &ns2);
-                __stcs(reinterpret_cast<unsigned int*>(D.c1 + (e0 >> 1)), c1);
+                if (!F1) __stcs(reinterpret_cast<unsigned int*>(D.c1 + (e0 >> 1)), c1);
                 __stcs(reinterpret_cast<unsigned int*>(D.c2 + (e0 >> 1)), c2);
                 if (g.j == 0) {
                     sm.scales[0][slot] = ns1;
@@ -315,11 +325,15 @@ step_kernel(const __grid_constant__ StepLaunch L) {
                 if (D.pc != nullptr) store_model_copy(D, e0, p);
             }
 
-            // re-encode m1 (adamw.py:764-771)
-            if (M1 != AW4_RTN) load_uniforms<M1>(u, D.d1, H.m1_key, H, D, e0, active);
-            float ns1;
-            const uint32_t c1 =
-                encode_block<M1>(sm.s1, r1, g, m1, amax1, u, 0, 0, H.sr_bias, H.eps, &ns1);
+            // re-encode m1 (adamw.py:764-771), or store the FP32 moment
+            float ns1 = 0.0f;
+            uint32_t c1 = 0;
+            if constexpr (F1) {
+                if (active) Elem<AW4_F32>::store8(D.c1, e0, m1);
+            } else {
+                if (M1 == AW4_SR_VALUE) load_uniforms<M1>(u, D.d1, H.m1_key, H, D, e0, active);
+                c1 = encode_block<M1>(sm.s1, r1, g, m1, amax1, u, 0, 0, H.sr_bias, H.eps, &ns1);
+            }
 
             // re-encode m2 (adamw.py:675-683 update-SR, 795-803 RTN + floor + EDEN)
             if (M2 != AW4_RTN) load_uniforms<M2>(u, D.d2, H.m2_key, H, D, e0, active);
@@ -328,7 +342,7 @@ step_kernel(const __grid_constant__ StepLaunch L) {
                 encode_block<M2>(sm.s2, r2, g, m2, amax2, u, zf2, L.eden, H.sr_bias, H.eps, &ns2);
 
             if (active) {
-                __stcs(reinterpret_cast<unsigned int*>(D.c1 + (e0 >> 1)), c1);
+                if (!F1) __stcs(reinterpret_cast<unsigned int*>(D.c1 + (e0 >> 1)), c1);
                 __stcs(reinterpret_cast<unsigned int*>(D.c2 + (e0 >> 1)), c2);
                 if (g.j == 0) {
                     sm.scales[0][slot] = ns1;
@@ -338,7 +352,7 @@ step_kernel(const __grid_constant__ StepLaunch L) {
         }
         // this warp's 8 scales per moment: lanes 0-7 m1, 8-15 m2
         __syncwarp();
-        if (lane < 16) {
+        if (lane < 16 && (!F1 || lane >= 8)) {
             const int k = lane & 7, mo = lane >> 3;
             const int tb = tile0 + 8 * warp + k;
             if (tb < D.nblocks) __stcs((mo ? D.s2 : D.s1) + tb, sm.scales[mo][8 * warp + k]);
@@ -417,6 +431,9 @@ template <int PT, int GT, bool GMC>
 static StepFn pick_m1(int m1, int m2) {
     if (m1 == AW4_RTN) return pick_m2<PT, GT, AW4_RTN, GMC>(m2);
     if (m1 == AW4_SR_VALUE) return pick_m2<PT, GT, AW4_SR_VALUE, GMC>(m2);
+    if constexpr (!GMC) {   // FP32 first moments next to a 4-bit second moment
+        if (m1 == AW4_FP32_MOMENT) return pick_m2<PT, GT, AW4_FP32_MOMENT, false>(m2);
+    }
     return nullptr;
 }
 
@@ -525,8 +542,11 @@ extern "C" int32_t aw4_step_quantized(const aw4_scheme* m1, const aw4_scheme* m2
                                       int32_t device, void* stream) {
     if (!m1 || !m2 || (n_tensors > 0 && (!tensors || !hypers)) || n_tensors < 0 || n_hypers < 0)
         return fail(AW4_ERR_INVALID, "aw4_step_quantized: null argument or negative count");
-    if (m1->round_mode != AW4_RTN && m1->round_mode != AW4_SR_VALUE)
-        return fail(AW4_ERR_UNSUPPORTED, "aw4_step_quantized: m1 rounding must be RTN or value SR");
+    if (m1->round_mode != AW4_RTN && m1->round_mode != AW4_SR_VALUE &&
+        m1->round_mode != AW4_FP32_MOMENT)
+        return fail(AW4_ERR_UNSUPPORTED,
+                    "aw4_step_quantized: m1 must be RTN, value SR or an FP32 moment");
+    const bool f1 = m1->round_mode == AW4_FP32_MOMENT;
     if (m2->round_mode < AW4_RTN || m2->round_mode > AW4_SR_UPDATE)
         return fail(AW4_ERR_INVALID, "aw4_step_quantized: bad m2 rounding mode");
     StepFn fn = pick_step(param_dtype, grad_dtype, m1->round_mode, m2->round_mode, false);
@@ -541,8 +561,12 @@ extern "C" int32_t aw4_step_quantized(const aw4_scheme* m1, const aw4_scheme* m2
             return fail(AW4_ERR_INVALID, "tensor %d: numel %lld is not a positive multiple of 128",
                         i, (long long)t.numel);
         if (t.numel == 0) continue;
-        if (!t.param || !t.grad || !t.m1_codes || !t.m1_scales || !t.m2_codes || !t.m2_scales)
+        if (!t.param || !t.grad || !t.m1_codes || (!t.m1_scales && !f1) || !t.m2_codes ||
+            !t.m2_scales)
             return fail(AW4_ERR_INVALID, "tensor %d: null buffer", i);
+        if (f1 && (!aligned(t.m1_codes, 16) || t.grad_multicast))
+            return fail(AW4_ERR_INVALID, "tensor %d: an FP32 m1 needs 16-byte aligned values and "
+                        "a local gradient", i);
         if (!aligned(t.param, 16) || !aligned(t.grad, 16) || !aligned(t.m1_codes, 4) ||
             !aligned(t.m2_codes, 4) || !aligned(t.m1_scales, 4) || !aligned(t.m2_scales, 4) ||
             (t.m1_draws && !aligned(t.m1_draws, 16)) || (t.m2_draws && !aligned(t.m2_draws, 16)))

@@ -205,9 +205,9 @@ class QuantizedAdamW(Optimizer):
                 "by the fused B200 step")
         if block_size is not None and block_size != 128:
             raise NotImplementedError("the fused B200 step uses 128-value quantization blocks")
-        if (m1_scheme == "fp32") != (m2_scheme == "fp32"):
-            raise NotImplementedError("mixed FP32/quantized moments are not implemented; use "
-                                      "4-bit schemes for both moments or 'fp32' for both")
+        if m2_scheme == "fp32" and m1_scheme != "fp32":
+            raise NotImplementedError("a 4-bit m1 next to an FP32 m2 is not implemented; use "
+                                      "'fp32' for m1 too, or a 4-bit m2")
         for s, moment in ((m1_scheme, "m1"), (m2_scheme, "m2")):
             if s == "fp32":
                 continue
@@ -454,6 +454,22 @@ class ZEEDENAdamW4Bit(QuantizedAdamW):
 # one step: gather tensors, then one launch per (device, dtypes, schemes)
 # ---------------------------------------------------------------------------
 
+_FP32_MOMENT = None
+
+
+def _kernel_scheme(mode: str):
+    """The prepared scheme of a quantized moment, or the FP32-moment mode
+    (an m1 kept as float32 values next to a 4-bit m2)."""
+    global _FP32_MOMENT
+    if mode != "fp32":
+        return prepared(mode)
+    if _FP32_MOMENT is None:
+        s = N.Scheme()
+        s.round_mode = N.FP32_MOMENT
+        _FP32_MOMENT = s
+    return _FP32_MOMENT
+
+
 def hyper_scalars(lr: float, beta1: float, beta2: float, eps: float, weight_decay: float,
                   step: int, next_bias: bool) -> dict:
     """Per-step float32 scalars, derived in float64 as adamw.py:557-564, 684-691
@@ -485,6 +501,9 @@ class _StepPlan:
             return
         stream = N.stream_handle(p.device)
         for key, scheme, e in (("m1", m1, False), ("m2", m2, eden)):
+            if scheme == "fp32":   # an FP32 m1 next to a 4-bit m2 (adamw.py:830-833)
+                st[key] = torch.zeros(p.shape, dtype=torch.float32, device=p.device)
+                continue
             codes = torch.empty(n // 2, dtype=torch.uint8, device=p.device)
             scales = torch.empty(n // 128, dtype=torch.float32, device=p.device)
             N.check(N.lib().aw4_init_zero_state(prepared(scheme), int(e), N.ptr(codes), N.ptr(scales),
@@ -527,7 +546,7 @@ class _StepPlan:
         if not quantized:
             self.fgroups.setdefault((p.device, pdt, gdt), []).append((p, g, st, hy))
             return
-        m1_sr = SCHEMES[m1].round_mode != N.RTN
+        m1_sr = m1 != "fp32" and SCHEMES[m1].round_mode != N.RTN
         m2_sr = SCHEMES[m2].round_mode != N.RTN
         d1 = d2 = None
         override = opt._draws_override
@@ -545,7 +564,7 @@ class _StepPlan:
         else:
             keys = (0, 0)
         # legacy one-code-per-byte state is repacked before the kernel reads it
-        for key in ("m1", "m2"):
+        for key in ("m1", "m2") if m1 != "fp32" else ("m2",):
             qs = st[f"{key}_quant_state"]
             if not getattr(qs, "packed", False):
                 codes = st[f"{key}_code"]
@@ -553,6 +572,12 @@ class _StepPlan:
                     st[f"{key}_code"] = pack_4bit_codes(codes.reshape(-1).contiguous())
                 qs.packed = True
             self._check_state(st, key, p)
+        if m1 == "fp32":
+            t1 = st.get("m1")
+            if (not torch.is_tensor(t1) or t1.dtype != torch.float32 or t1.numel() != p.numel()
+                    or t1.device != p.device or not t1.is_contiguous()):
+                raise RuntimeError("optimizer state m1 of an FP32 first moment must be a "
+                                   f"contiguous float32 tensor of {p.numel()} values")
         self.qgroups.setdefault((p.device, pdt, gdt, m1, m2, eden), []).append(
             (p, g, st, hy, keys, ordinal, d1, d2))
 
@@ -659,7 +684,9 @@ class _StepPlan:
                                           hy["sqrt_bc2"], hy["eps"], hy["sr_bias"], hy["step"],
                                           keys[0], keys[1]))
                 tensors.append(N.QTensor(
-                    N.ptr(p), N.ptr(g), N.ptr(st["m1_code"]), N.ptr(st["m1_quant_state"].absmax),
+                    N.ptr(p), N.ptr(g),
+                    N.ptr(st["m1"]) if m1 == "fp32" else N.ptr(st["m1_code"]),
+                    None if m1 == "fp32" else N.ptr(st["m1_quant_state"].absmax),
                     N.ptr(st["m2_code"]), N.ptr(st["m2_quant_state"].absmax), N.ptr(d1), N.ptr(d2),
                     p.numel(), 0, ordinal, hindex[hk]))
             tarr = (N.QTensor * len(tensors))(*tensors)
@@ -669,7 +696,8 @@ class _StepPlan:
                 ev0 = torch.cuda.Event(enable_timing=True)
                 ev1 = torch.cuda.Event(enable_timing=True)
                 ev0.record(torch.cuda.current_stream(dev))
-            N.check(N.lib().aw4_step_quantized(prepared(m1), prepared(m2), int(eden), pdt, gdt, tarr,
+            N.check(N.lib().aw4_step_quantized(_kernel_scheme(m1), prepared(m2), int(eden), pdt,
+                                               gdt, tarr,
                                                len(tensors), harr, len(hypers), 0, dev.index,
                                                N.stream_handle(dev)), "aw4_step_quantized")
             if timing is not None:

@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define AW4_ABI_VERSION 4
+#define AW4_ABI_VERSION 5
 #define AW4_BLOCK 128          /* elements per quantization block (4-bit default) */
 #define AW4_LUT_BINS 1024      /* maximum uniform bins over [-1, 1] for the rounding search */
 
@@ -54,7 +54,11 @@ typedef enum aw4_dtype { AW4_F32 = 0, AW4_BF16 = 1, AW4_F16 = 2 } aw4_dtype;
 typedef enum aw4_round {
     AW4_RTN = 0,         /* nearest level, ties up   (quantization.py:254-272) */
     AW4_SR_VALUE = 1,    /* value-unbiased SR        (quantization.py:286-315) */
-    AW4_SR_UPDATE = 2    /* preconditioner-space SR  (quantization.py:327-377) */
+    AW4_SR_UPDATE = 2,   /* preconditioner-space SR  (quantization.py:327-377) */
+    AW4_FP32_MOMENT = 3  /* m1 only: kept as float32 values, not quantized (the "fp32"
+                          * scheme next to a 4-bit m2, adamw.py:510-521, 830-833); the
+                          * tensor's m1_codes points to numel float32 values (16-byte
+                          * aligned) and m1_scales is unused */
 } aw4_round;
 
 /* A 4-bit moment scheme prepared for the kernels (host memory, filled by

@@ -3,7 +3,7 @@ interchange, made by running the REFERENCE (nubank/adamw4bit, eager path,
 optimized=False) on the CPU.
 
     python tests/golden/make_golden_configs.py --reference <reference checkout> \
-        [--only c3,c4,c5,ckpt] [--threads N]
+        [--only c3,c4,c5,ckpt,mixed] [--threads N]
 
 Inputs come from tests/synth.py (hash-indexed pool gathers that are
 bit-identical on the CPU and on CUDA), so the GPU tests rebuild every
@@ -268,6 +268,49 @@ def checkpoint_fixture(ref, name: str, recipe: str, seed, k: int = 3, more: int 
     print(f"checkpoint fixture {name} written", flush=True)
 
 
+def moment_digests(opt, params) -> dict:
+    """Per moment: packed codes and scales when the moment is quantized,
+    else its FP32 values (all tensors concatenated in parameter order)."""
+    d = {k: Digest() for k in ("m1_code", "m1_absmax", "m2_code", "m2_absmax", "f_m1", "f_m2")}
+    for p in params:
+        st = opt.state[p]
+        for m in ("m1", "m2"):
+            if f"{m}_code" in st:
+                d[f"{m}_code"].add(st[f"{m}_code"])
+                d[f"{m}_absmax"].add(st[f"{m}_quant_state"].absmax)
+            else:
+                d[f"f_{m}"].add(st[m])
+    return {k: v.hex() for k, v in d.items()}
+
+
+def mixed_fixture(ref, name: str, m2_scheme: str, eden: bool, seed, steps: int = 6):
+    """FP32 first moments next to a 4-bit second moment (the reference
+    resolves each moment's scheme on its own, adamw.py:510-521)."""
+    shapes = [(64, 512), (768,), (32, 128)]
+    params = [torch.nn.Parameter(S.init_param(s, i, torch.float32, "cpu"))
+              for i, s in enumerate(shapes)]
+    kw = dict(lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1,
+              m1_quant_scheme="fp32", m2_quant_scheme=m2_scheme, use_eden_m2=eden)
+    if seed is not None:
+        kw["quant_rng_seed"] = seed
+    opt = ref.QuantizedAdamW(params, **kw)
+    meta = {"name": name, "shapes": [list(s) for s in shapes], "m1_scheme": "fp32",
+            "m2_scheme": m2_scheme, "eden": eden, "quant_rng_seed": seed, "steps": steps,
+            "grad_std": 1e-3, "per_step": []}
+    arrays = {}
+    for t in range(1, steps + 1):
+        for i, p in enumerate(params):
+            p.grad = S.grad(p.shape, i, t, 1e-3, torch.float32, "cpu")
+        opt.step()
+        meta["per_step"].append({"step": t, **moment_digests(opt, params)})
+    for i, p in enumerate(params):
+        arrays[f"s{steps}_p{i}"] = p.detach().numpy().copy()
+    with open(os.path.join(HERE, f"mixed_{name}.json"), "w") as fh:
+        json.dump(meta, fh, indent=1)
+    np.savez_compressed(os.path.join(HERE, f"mixed_{name}.npz"), **arrays)
+    print(f"mixed fixture {name} written", flush=True)
+
+
 def main() -> None:
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", required=True, help="root of the reference checkout")
@@ -281,7 +324,10 @@ def main() -> None:
 
     f32, bf16 = torch.float32, torch.bfloat16
     for item in args.only.split(","):
-        if item == "ckpt":
+        if item == "mixed":
+            mixed_fixture(ref, "fp32m1_zipsr", "dyn4_upd_sr_fp32read", False, 11)
+            mixed_fixture(ref, "fp32m1_zeeden", "dyn4_nz", True, None)
+        elif item == "ckpt":
             checkpoint_fixture(ref, "zeeden", "ze-eden", None)
             checkpoint_fixture(ref, "zipsr", "zip-sr", 4321)
         elif item == "c3":

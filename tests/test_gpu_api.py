@@ -399,3 +399,85 @@ def test_aliased_moment_state_after_load_is_detached():
         assert torch.equal(pa.detach(), pb.detach())
         for key in ("m1_code", "m2_code"):
             assert torch.equal(opt_a.state[pa][key], opt_b.state[pb][key])
+
+
+@pytest.mark.parametrize("scheme", ["lin4_upd_sr_fp32read", "dyn4_upd_sr_fp32read",
+                                    "dyn4_lookahead_sr", "dyn4_upd_sr_fp32read_nextbc"])
+def test_fp32_m1_first_step_matches_adamw_and_stores_quantized_m2(scheme):
+    """Reference KAT tests/quantization/test_dyn4_la_upd_sr.py:151-191: an FP32
+    m1 next to a 4-bit fp32read m2; the first step equals torch's AdamW, m2 is
+    stored packed and decodes to finite values."""
+    values = torch.linspace(-1.0, 1.0, steps=4096, device=DEV)
+    grad = torch.linspace(-0.5, 0.5, steps=4096, device=DEV)
+    p_q = torch.nn.Parameter(values.clone())
+    p_f = torch.nn.Parameter(values.clone())
+    kwargs = {"lr": 1e-3, "weight_decay": 0.0, "betas": (0.9, 0.95), "eps": 1e-8}
+    opt_q = AdamW8bit([p_q], **kwargs, m1_quant_scheme="fp32", m2_quant_scheme=scheme,
+                      block_size=128)
+    opt_f = torch.optim.AdamW([p_f], **kwargs)
+    p_q.grad = grad.clone()
+    p_f.grad = grad.clone()
+    opt_q.step()
+    opt_f.step()
+    torch.testing.assert_close(p_q, p_f, rtol=1e-6, atol=1e-6)
+    state = opt_q.state[p_q]
+    assert "m2_code" in state and "m2_quant_state" in state and "m2" not in state
+    assert state["m1"].dtype == torch.float32 and "m1_code" not in state
+    saved = Q.dequantize(state["m2_code"], state["m2_quant_state"], mode=scheme)
+    assert saved.shape == p_q.shape and torch.isfinite(saved).all()
+
+
+@pytest.mark.parametrize("name", ["fp32m1_zipsr", "fp32m1_zeeden"])
+def test_fp32_m1_with_4bit_m2_matches_reference_trajectory(name):
+    """An FP32 m1 next to a 4-bit m2 (the reference resolves each moment's
+    scheme on its own, adamw.py:510-521), 6 steps: the FP32 moments, the m2
+    codes and scales bit-exact with the reference's own run (its draws for
+    the SR scheme), parameters within rtol 1e-6."""
+    import hashlib
+    import json
+    import os
+
+    from tests import synth as S
+    golden = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
+    with open(os.path.join(golden, f"mixed_{name}.json")) as f:
+        meta = json.load(f)
+    arrays = dict(np.load(os.path.join(golden, f"mixed_{name}.npz")))
+    shapes = [tuple(s) for s in meta["shapes"]]
+    params = [torch.nn.Parameter(S.init_param(s, i, torch.float32, DEV)) for i, s in enumerate(shapes)]
+    kw = dict(lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, m1_quant_scheme="fp32",
+              m2_quant_scheme=meta["m2_scheme"], use_eden_m2=meta["eden"])
+    seed = meta["quant_rng_seed"]
+    if seed is not None:
+        kw["quant_rng_seed"] = seed
+    opt = QuantizedAdamW(params, **kw)
+    sr = Q.SCHEMES[meta["m2_scheme"]].round_mode != _native.RTN
+    gen = torch.Generator().manual_seed((seed + G.M2_OFFSET) % ((1 << 63) - 1)) if sr else None
+    for t in range(1, meta["steps"] + 1):
+        for i, p in enumerate(params):
+            p.grad = S.grad(p.shape, i, t, meta["grad_std"], torch.float32, DEV)
+        if gen is not None:
+            draws = {}
+            for p in params:
+                if p.numel() >= 4096 and p.numel() % 128 == 0:
+                    rows = (p.numel() // 128, 128)
+                    if t == 1:
+                        torch.rand(rows, generator=gen)            # zero-state init
+                    draws[id(p)] = (None, torch.rand(rows, generator=gen).reshape(-1).to(DEV))
+            opt._draws_override = draws
+        opt.step()
+        hs = {k: hashlib.sha256() for k in ("m1_code", "m1_absmax", "m2_code", "m2_absmax",
+                                            "f_m1", "f_m2")}
+        for p in params:
+            st = opt.state[p]
+            for m in ("m1", "m2"):
+                if f"{m}_code" in st:
+                    hs[f"{m}_code"].update(st[f"{m}_code"].cpu().numpy().tobytes())
+                    hs[f"{m}_absmax"].update(st[f"{m}_quant_state"].absmax.cpu().numpy().tobytes())
+                else:
+                    hs[f"f_{m}"].update(st[m].cpu().numpy().tobytes())
+        rec = meta["per_step"][t - 1]
+        for k, h in hs.items():
+            assert h.hexdigest() == rec[k], f"{name} step {t}: {k}"
+    for i, p in enumerate(params):
+        np.testing.assert_allclose(p.detach().cpu().numpy(), arrays[f"s{meta['steps']}_p{i}"],
+                                   rtol=1e-6, atol=1e-9)

@@ -18,8 +18,10 @@ draws are the reference's: its CPU generators, replayed in its order and fed
 through the optimizer's draws hook.  Every step must reproduce the
 reference's SHA-256 digests of all packed codes, all block scales and all
 FP32 moments.  Parameters are compared per tensor (float64 sums) and on
-strided samples: FP32 within rtol 1e-6 (the reference's CPU square root, MKL,
-is not correctly rounded, so parameters cannot be bit-exact); BF16 bit-equal
+strided samples: FP32 within rtol 1e-6, with an absolute floor of 1e-6 of
+the sample's mean magnitude for values near zero (the reference's CPU square
+root, MKL, is not correctly rounded, so parameters cannot be bit-exact and
+its 1e-7 relative differences accumulate over 100 steps); BF16 bit-equal
 except where that 1e-7 relative difference crosses a BF16 rounding boundary,
 which may move a parameter by one BF16 ulp.
 
@@ -204,7 +206,11 @@ def _run_config(name, *, check_every=1):
             del flat
             want = arrays[key]
             if p_dt == torch.float32:
-                np.testing.assert_allclose(sample, want, rtol=PARAM_RTOL, atol=1e-9,
+                # relative to the values and to the parameters' scale: a value
+                # near zero carries the drift of its many updates in absolute
+                # terms, never more than 1e-6 of the typical magnitude
+                np.testing.assert_allclose(sample, want, rtol=PARAM_RTOL,
+                                           atol=PARAM_RTOL * float(np.abs(want).mean()),
                                            err_msg=f"{name} step {t}")
             else:
                 diff = sample != want

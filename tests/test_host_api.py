@@ -51,12 +51,18 @@ def test_constructor_validation_matches_reference_messages(kwargs, match):
     dict(record_preconditioner_steps=[1], m1_quant_scheme="nf4", m2_quant_scheme="dyn4_nz"),
     dict(m1_quant_scheme="linear", m2_quant_scheme="linear"),
     dict(m1_quant_scheme="nf4", m2_quant_scheme="dyn4_upd_sr"),
-    dict(m1_quant_scheme="fp32", m2_quant_scheme="dyn4_nz"),
+    dict(m1_quant_scheme="nf4", m2_quant_scheme="fp32"),
     dict(m1_quant_scheme="nf4", m2_quant_scheme="dyn4_nz", block_size=64),
 ])
 def test_out_of_scope_options_fail_loudly(kwargs):
     with pytest.raises(NotImplementedError):
         QuantizedAdamW([_p()], **kwargs)
+
+
+def test_fp32_m1_next_to_a_4bit_m2_is_accepted():
+    """The reference resolves each moment's scheme on its own (adamw.py:510-521)."""
+    opt = QuantizedAdamW([_p()], m1_quant_scheme="fp32", m2_quant_scheme="dyn4_upd_sr_fp32read")
+    assert opt.param_groups[0]["m1_quant_scheme"] == "fp32"
 
 
 def test_recipes_fix_the_paper_schemes():
