@@ -243,15 +243,21 @@ step_kernel(const __grid_constant__ StepLaunch L) {
                 }
                 if constexpr (F1) {
                     Elem<AW4_F32>::load8(D.c1, e0, m1);
+                    w2 = __ldcs(reinterpret_cast<const unsigned int*>(D.c2 + (e0 >> 1)));
+                    s2 = __ldcs(D.s2 + blk);
                 } else {
                     w1 = __ldcs(reinterpret_cast<const unsigned int*>(D.c1 + (e0 >> 1)));
+                    w2 = __ldcs(reinterpret_cast<const unsigned int*>(D.c2 + (e0 >> 1)));
                     s1 = __ldcs(D.s1 + blk);
+                    s2 = __ldcs(D.s2 + blk);
                 }
-                w2 = __ldcs(reinterpret_cast<const unsigned int*>(D.c2 + (e0 >> 1)));
-                s2 = __ldcs(D.s2 + blk);
             } else {
 #pragma unroll
-                for (int i = 0; i < 8; ++i) p[i] = gr[i] = m1[i] = 0.0f;
+                for (int i = 0; i < 8; ++i) p[i] = gr[i] = 0.0f;
+                if constexpr (F1) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) m1[i] = 0.0f;
+                }
             }
             // Packed f32x2 arithmetic throughout: multiplies, FMAs, and
             // additions as fma(a, one, b) (no multiply can be fused into them).
@@ -288,24 +294,31 @@ step_kernel(const __grid_constant__ StepLaunch L) {
                 vadd8(p, q, p, one);                 // p.addcdiv_(m1, den, -lr/bc1)
                 Elem<PT>::store8(D.param, e0, p);
                 if (D.pc != nullptr) store_model_copy(D, e0, p);
-                float ns1 = 0.0f, ns2;
-                uint32_t c1 = 0;
                 if constexpr (F1) {
                     Elem<AW4_F32>::store8(D.c1, e0, m1);   // the FP32 moment itself
+                    if (M2 != AW4_RTN) load_uniforms<M2>(u, D.d2, H.m2_key, H, D, e0, true);
+                    float ns2;
+                    const uint32_t c2 =
+                        encode_fast<M2>(sm.s2, r2, g, m2, sc2, u, zf2, L.eden, H.sr_bias, H.eps,
+                                        H.sr_rbias, one, &ns2);
+                    __stcs(reinterpret_cast<unsigned int*>(D.c2 + (e0 >> 1)), c2);
+                    if (g.j == 0) sm.scales[1][slot] = ns2;
                 } else {
                     if (M1 == AW4_SR_VALUE) load_uniforms<M1>(u, D.d1, H.m1_key, H, D, e0, true);
-                    c1 = encode_fast<M1>(sm.s1, r1, g, m1, sc1, u, 0, 0, H.sr_bias, H.eps,
-                                         H.sr_rbias, one, &ns1);
-                }
-                if (M2 != AW4_RTN) load_uniforms<M2>(u, D.d2, H.m2_key, H, D, e0, true);
-                const uint32_t c2 =
-                    encode_fast<M2>(sm.s2, r2, g, m2, sc2, u, zf2, L.eden, H.sr_bias, H.eps,
-                                    H.sr_rbias, one, &ns2);
-                if (!F1) __stcs(reinterpret_cast<unsigned int*>(D.c1 + (e0 >> 1)), c1);
-                __stcs(reinterpret_cast<unsigned int*>(D.c2 + (e0 >> 1)), c2);
-                if (g.j == 0) {
-                    sm.scales[0][slot] = ns1;
-                    sm.scales[1][slot] = ns2;
+                    float ns1, ns2;
+                    const uint32_t c1 =
+                        encode_fast<M1>(sm.s1, r1, g, m1, sc1, u, 0, 0, H.sr_bias, H.eps,
+                                        H.sr_rbias, one, &ns1);
+                    if (M2 != AW4_RTN) load_uniforms<M2>(u, D.d2, H.m2_key, H, D, e0, true);
+                    const uint32_t c2 =
+                        encode_fast<M2>(sm.s2, r2, g, m2, sc2, u, zf2, L.eden, H.sr_bias, H.eps,
+                                        H.sr_rbias, one, &ns2);
+                    __stcs(reinterpret_cast<unsigned int*>(D.c1 + (e0 >> 1)), c1);
+                    __stcs(reinterpret_cast<unsigned int*>(D.c2 + (e0 >> 1)), c2);
+                    if (g.j == 0) {
+                        sm.scales[0][slot] = ns1;
+                        sm.scales[1][slot] = ns2;
+                    }
                 }
                 continue;
             }
@@ -325,28 +338,34 @@ step_kernel(const __grid_constant__ StepLaunch L) {
                 if (D.pc != nullptr) store_model_copy(D, e0, p);
             }
 
-            // re-encode m1 (adamw.py:764-771), or store the FP32 moment
-            float ns1 = 0.0f;
-            uint32_t c1 = 0;
+            // re-encode m2 (adamw.py:675-683 update-SR, 795-803 RTN + floor + EDEN)
+            // after m1 (adamw.py:764-771), or next to the FP32 moment itself
             if constexpr (F1) {
                 if (active) Elem<AW4_F32>::store8(D.c1, e0, m1);
+                if (M2 != AW4_RTN) load_uniforms<M2>(u, D.d2, H.m2_key, H, D, e0, active);
+                float ns2;
+                const uint32_t c2 = encode_block<M2>(sm.s2, r2, g, m2, amax2, u, zf2, L.eden,
+                                                     H.sr_bias, H.eps, &ns2);
+                if (active) {
+                    __stcs(reinterpret_cast<unsigned int*>(D.c2 + (e0 >> 1)), c2);
+                    if (g.j == 0) sm.scales[1][slot] = ns2;
+                }
             } else {
                 if (M1 == AW4_SR_VALUE) load_uniforms<M1>(u, D.d1, H.m1_key, H, D, e0, active);
-                c1 = encode_block<M1>(sm.s1, r1, g, m1, amax1, u, 0, 0, H.sr_bias, H.eps, &ns1);
-            }
-
-            // re-encode m2 (adamw.py:675-683 update-SR, 795-803 RTN + floor + EDEN)
-            if (M2 != AW4_RTN) load_uniforms<M2>(u, D.d2, H.m2_key, H, D, e0, active);
-            float ns2;
-            const uint32_t c2 =
-                encode_block<M2>(sm.s2, r2, g, m2, amax2, u, zf2, L.eden, H.sr_bias, H.eps, &ns2);
-
-            if (active) {
-                if (!F1) __stcs(reinterpret_cast<unsigned int*>(D.c1 + (e0 >> 1)), c1);
-                __stcs(reinterpret_cast<unsigned int*>(D.c2 + (e0 >> 1)), c2);
-                if (g.j == 0) {
-                    sm.scales[0][slot] = ns1;
-                    sm.scales[1][slot] = ns2;
+                float ns1;
+                const uint32_t c1 =
+                    encode_block<M1>(sm.s1, r1, g, m1, amax1, u, 0, 0, H.sr_bias, H.eps, &ns1);
+                if (M2 != AW4_RTN) load_uniforms<M2>(u, D.d2, H.m2_key, H, D, e0, active);
+                float ns2;
+                const uint32_t c2 = encode_block<M2>(sm.s2, r2, g, m2, amax2, u, zf2, L.eden,
+                                                     H.sr_bias, H.eps, &ns2);
+                if (active) {
+                    __stcs(reinterpret_cast<unsigned int*>(D.c1 + (e0 >> 1)), c1);
+                    __stcs(reinterpret_cast<unsigned int*>(D.c2 + (e0 >> 1)), c2);
+                    if (g.j == 0) {
+                        sm.scales[0][slot] = ns1;
+                        sm.scales[1][slot] = ns2;
+                    }
                 }
             }
         }

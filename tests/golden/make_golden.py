@@ -6,10 +6,11 @@ the reference at run time:
 
     python tests/golden/make_golden.py --reference <path to the reference checkout>
 
-Every optimizer trajectory uses the reference's eager path (optimized=False),
-the parity oracle named by the survey.  Inputs are seeded synthetic tensors
-shaped like the benchmark configurations; gradients are regenerated in the
-tests from the same torch CPU generator recipe (recorded in each fixture,
+Every optimizer trajectory uses the reference's eager path (optimized=False):
+its optimized=True path draws a different number of SR uniforms at state
+initialisation, so the eager path is the one parity is defined against.
+Inputs are seeded synthetic tensors shaped like the benchmark configurations;
+gradients are regenerated in the tests from the same torch CPU generator recipe (recorded in each fixture,
 with a checksum of every step's gradient to detect drift).
 """
 
