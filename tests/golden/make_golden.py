@@ -10,8 +10,9 @@ Every optimizer trajectory uses the reference's eager path (optimized=False):
 its optimized=True path draws a different number of SR uniforms at state
 initialisation, so the eager path is the one parity is defined against.
 Inputs are seeded synthetic tensors shaped like the benchmark configurations;
-gradients are regenerated in the tests from the same torch CPU generator recipe (recorded in each fixture,
-with a checksum of every step's gradient to detect drift).
+gradients are regenerated in the tests from the same torch CPU generator
+recipe (recorded in each fixture, with a checksum of every step's gradient to
+detect drift).
 """
 
 from __future__ import annotations
