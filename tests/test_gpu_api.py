@@ -481,3 +481,48 @@ def test_fp32_m1_with_4bit_m2_matches_reference_trajectory(name):
     for i, p in enumerate(params):
         np.testing.assert_allclose(p.detach().cpu().numpy(), arrays[f"s{meta['steps']}_p{i}"],
                                    rtol=1e-6, atol=1e-9)
+
+
+def test_philox_trajectory_is_distributionally_equal_to_reference_draws():
+    """The north star's bar for SR under Philox, at trajectory level: BASELINE
+    configuration 2 (one 4096x4096 FP32 tensor, ZIP-SR, 10 steps) under 16
+    seeds, once with the in-kernel Philox stream and once with the
+    reference's own draws (its CPU generator seeded (seed + 0x5E6F7789),
+    adamw.py:281-324, fed through the draws hook).  Per seed: the mean and
+    variance of the dequantized m2 and the mean Adam preconditioner
+    1/(sqrt(m2/bc2) + eps).  The two samples of 16 must agree: a two-sample
+    t statistic below 4 for each statistic, and variances across seeds
+    within a factor 6.5 of each other (F(15, 15) at 0.05 %).  The seeds are
+    fixed, so the outcome is the same on every run."""
+    import math
+
+    from tests import synth as S
+    shape, steps, seeds = (4096, 4096), 10, range(100, 116)
+    n = shape[0] * shape[1]
+    bc2 = 1 - 0.95 ** steps
+    stats = {"philox": [], "reference": []}
+    for mode in stats:
+        for seed in seeds:
+            p = torch.nn.Parameter(S.init_param(shape, 0, torch.float32, DEV))
+            opt = ZIPSRAdamW4Bit([p], quant_rng_seed=seed)
+            gen = (torch.Generator().manual_seed((seed + G.M2_OFFSET) % ((1 << 63) - 1))
+                   if mode == "reference" else None)
+            for t in range(1, steps + 1):
+                p.grad = S.grad(shape, 0, t, 1e-3, torch.float32, DEV)
+                if gen is not None:
+                    if t == 1:
+                        torch.rand((n // 128, 128), generator=gen)      # zero-state init
+                    d2 = torch.rand((n // 128, 128), generator=gen).reshape(-1).to(DEV)
+                    opt._draws_override = {id(p): (None, d2)}
+                opt.step()
+            st = opt.state[p]
+            m2 = Q.dequantize(st["m2_code"], st["m2_quant_state"],
+                              mode="dyn4_upd_sr_fp32read").double()
+            pre = 1.0 / (torch.sqrt(m2 / bc2) + 1e-8)
+            stats[mode].append([m2.mean().item(), m2.var().item(), pre.mean().item()])
+    a, b = np.array(stats["philox"]), np.array(stats["reference"])
+    for k, what in enumerate(("mean of m2", "variance of m2", "mean preconditioner")):
+        va, vb = a[:, k].var(ddof=1), b[:, k].var(ddof=1)
+        tstat = abs(a[:, k].mean() - b[:, k].mean()) / math.sqrt(va / len(a) + vb / len(b))
+        assert tstat < 4.0, (what, tstat, a[:, k].mean(), b[:, k].mean())
+        assert 1 / 6.5 < va / vb < 6.5, (what, va, vb)
