@@ -276,11 +276,12 @@ step_kernel(const __grid_constant__ StepLaunch L) {
 
             // One warp-uniform decision per sub-block: when every lane meets the
             // fast preconditions the rest runs without per-lane branches.
-            const float sc1 = max_nan(group_max16(amax1), kScaleFloor);
+            // (an FP32 m1 has no block scale: 0 passes the divisor bound below)
+            const float sc1 = F1 ? 0.0f : max_nan(group_max16(amax1), kScaleFloor);
             const float gmax2 = group_max16(amax2);
             const float sc2 = max_nan(gmax2, kScaleFloor);
             bool ok = active && amax1 <= H.m1_fast_max && amax2 <= H.m2_fast_max &&
-                      (F1 || sc1 <= kMarksteinMaxDivisor) && sc2 <= kMarksteinMaxDivisor &&
+                      sc1 <= kMarksteinMaxDivisor && sc2 <= kMarksteinMaxDivisor &&
                       (gmax2 >= kScaleFloor || !L.eden);
             ok = none_tiny_warp(nt, ok);
             if (M1 == AW4_SR_VALUE) ok = none_tiny_warp(m1, ok);
