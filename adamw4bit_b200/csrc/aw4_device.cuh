@@ -389,6 +389,47 @@ __device__ __forceinline__ void load8_reduce<AW4_F16>(const void* base, int64_t 
     }
 }
 
+// The same reduction in two halves, so a caller can issue the next values'
+// reduction before computing with the current ones: issue8_reduce starts the
+// multimem.ld_reduce of 8 values into raw words (8 for FP32, 4 for 16-bit
+// types), finish8_reduce widens them.  The loads are relaxed, system scope,
+// ordered after the ranks' writes by the caller's cross-rank barrier.
+template <int DT>
+__device__ __forceinline__ void issue8_reduce(const void* base, int64_t e, uint32_t w[8]) {
+    if constexpr (DT == AW4_F32) {
+        const float* p = static_cast<const float*>(base) + e;
+        asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]) : "l"(p) : "memory");
+        asm volatile("multimem.ld_reduce.relaxed.sys.global.add.v4.f32 {%0, %1, %2, %3}, [%4];"
+                     : "=r"(w[4]), "=r"(w[5]), "=r"(w[6]), "=r"(w[7]) : "l"(p + 4) : "memory");
+    } else if constexpr (DT == AW4_BF16) {
+        const uint16_t* p = static_cast<const uint16_t*>(base) + e;
+        asm volatile(
+            "multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+            : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]) : "l"(p) : "memory");
+    } else {
+        const uint16_t* p = static_cast<const uint16_t*>(base) + e;
+        asm volatile(
+            "multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.f16x2 {%0, %1, %2, %3}, [%4];"
+            : "=r"(w[0]), "=r"(w[1]), "=r"(w[2]), "=r"(w[3]) : "l"(p) : "memory");
+    }
+}
+template <int DT>
+__device__ __forceinline__ void finish8_reduce(const uint32_t w[8], float v[8]) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+        if constexpr (DT == AW4_F32) {
+            v[k] = __uint_as_float(w[k]);
+        } else if constexpr (DT == AW4_BF16) {   // element 2j in the low half of word j
+            v[k] = (k & 1) ? __uint_as_float(w[k >> 1] & 0xffff0000u)
+                           : __uint_as_float(w[k >> 1] << 16);
+        } else {
+            v[k] = __half2float(__ushort_as_half(
+                (unsigned short)((k & 1) ? (w[k >> 1] >> 16) : (w[k >> 1] & 0xffffu))));
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------
 // Philox4x32-10 (Salmon, Moraes, Dror, Shaw, SC'11).  Counter layout:
 // (e/4 low word, e/4 high word, step, ordinal); key = 64-bit stream key;

@@ -223,20 +223,34 @@ step_kernel(const __grid_constant__ StepLaunch L) {
         const KDesc& D = L.t[ti];
         const HyperDev& H = L.h;
         const int tile0 = (tile - D.tile_begin) * kStepBlocksPerTile;
+        // ZeRO-2: each sub-block's gradient sums are requested from the
+        // switch one sub-block ahead, so their round trip overlaps the math
+        uint32_t gnext[8];
+        if constexpr (GMC) {
+            const int blk = tile0 + 8 * warp + h;
+            if (blk < D.nblocks) issue8_reduce<GT>(D.grad, (int64_t)blk * kBlock + 8 * g.j, gnext);
+        }
 #pragma unroll 1
         for (int sb = 0; sb < kSubBlocks; ++sb) {
             const int slot = 8 * warp + 2 * sb + h;   // block within the tile: 8 per warp
             const int blk = tile0 + slot;
             const bool active = blk < D.nblocks;
             const int64_t e0 = (int64_t)blk * kBlock + 8 * g.j;
+            uint32_t gcur[8];
+            if constexpr (GMC) {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) gcur[k] = gnext[k];
+                if (sb + 1 < kSubBlocks && blk + 2 < D.nblocks)
+                    issue8_reduce<GT>(D.grad, e0 + 2 * kBlock, gnext);
+            }
 
             float p[8], gr[8], m1[8], m2[8];
             uint32_t w1 = 0, w2 = 0;
             float s1 = 0.0f, s2 = 0.0f;
             if (active) {
                 Elem<PT>::load8(D.param, e0, p);
-                if (GMC) {   // grad is a multicast address: the sum over ranks
-                    load8_reduce<GT>(D.grad, e0, gr);
+                if constexpr (GMC) {   // grad is a multicast address: the sum over ranks
+                    finish8_reduce<GT>(gcur, gr);
                     vmuls8(gr, gr, H.grad_scale);
                 } else {
                     Elem<GT>::load8(D.grad, e0, gr);
