@@ -363,6 +363,22 @@ def reference_cpu_rates(steps: int) -> dict:
     return out
 
 
+def rank_identities(world: int, dev) -> list | None:
+    """Each rank's GPU (name, PCI bus id) and the NCCL version, gathered over
+    the process group: the line shows which devices took part."""
+    if world == 1:
+        return None
+    import torch.distributed as dist
+    props = torch.cuda.get_device_properties(dev)
+    me = {"rank": dist.get_rank(), "device": props.name,
+          "pci_bus_id": f"{props.pci_domain_id:04x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}",
+          "nccl": ".".join(str(v) for v in torch.cuda.nccl.version()),
+          "nccl_nvls_enable": os.environ.get("NCCL_NVLS_ENABLE", "default")}
+    out = [None] * world
+    dist.all_gather_object(out, me)
+    return out
+
+
 def timed_steps(opt, steps: int, warmup: int) -> tuple[float, float, float]:
     """Runs warm-up then `steps` optimizer steps; returns (device ms per step,
     fused-kernel ms per step, values updated per step)."""
@@ -503,6 +519,7 @@ def run_ours(args, rank, world, local):
                 "values_per_launch": int(per_launch_elems)}
 
     e2e = run_e2e(args, opt, dev, world, total) if args.e2e_steps > 0 else None
+    ranks = rank_identities(world, dev)
     gather_mode = opt.gather_mode
     del opt, params, grads
     torch.cuda.empty_cache()
@@ -534,6 +551,7 @@ def run_ours(args, rank, world, local):
                 "clocks": clocks, "gpu_launches": int(launches),
                 "e2e": e2e}
         if world > 1:
+            line["ranks"] = ranks
             # every GPU receives the whole model minus its own shard each step
             nv = (world - 1) / world * total * (2 if master else 4)
             line["gather"] = {"ingress_bytes_per_gpu": nv,
