@@ -41,3 +41,17 @@ def test_reference_arm_prints_one_contract_line():
     assert rec["value"] > 0 and rec["higher_is_better"] is True
     assert rec["e2e"]["h2d_bytes_per_step"] == 0 and rec["e2e"]["d2h_bytes_per_step"] == 0
     assert rec["cpu_baseline"]["kind"] in ("port", "reference")
+
+
+def test_algorithmic_bytes_per_value():
+    """The roofline's bytes per value: parameter read + write, gradient read,
+    m1/m2 packed codes read + write (0.5 B each way each) and block scales
+    (2 moments x 4 B read + write per 128 values), plus the BF16 model copy
+    when FP32 master weights are kept."""
+    assert bench.B_STATE == 2.125
+    assert bench.bytes_per_value(4, 4, False) == 14.125      # configs 1-3
+    assert bench.bytes_per_value(2, 2, False) == 8.125       # config 4
+    assert bench.bytes_per_value(4, 2, False) == 12.125      # config 5, drop-in API
+    assert bench.bytes_per_value(4, 2, True) == bench.B_PER_ELEM == 14.125   # bench value
+    assert len(bench.llama_1b_shapes()) == 147
+    assert sum(int(torch.Size(s).numel()) for s in bench.llama_1b_shapes()) == 852_559_872
