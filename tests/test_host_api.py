@@ -144,6 +144,19 @@ def test_hyper_scalars_are_float32_roundings_of_float64_math():
     assert h2["sr_bias"] == float(np.float32(1 - 0.95 ** 4))
 
 
+@pytest.mark.parametrize("scheme,bias_step", [
+    ("lin4_upd_sr_fp32read", 1), ("dyn4_upd_sr_fp32read", 1),
+    ("dyn4_lookahead_sr", 2), ("dyn4_upd_sr_fp32read_nextbc", 2)])
+def test_update_sr_storage_bias_correction(scheme, bias_step):
+    """Reference tests/quantization/test_dyn4_la_upd_sr.py:240-275: at t = 1
+    the fp32-read schemes store against c_t = 1 - beta2^t, the lookahead SR
+    scheme and its nextbc alias against c_{t+1}; the kernel receives that
+    value as the float32 sr_bias of the step's scalars."""
+    from adamw4bit_b200.quantization import SCHEMES
+    h = hyper_scalars(1e-3, 0.9, 0.95, 1e-8, 0.0, 1, SCHEMES[scheme].next_bias)
+    assert h["sr_bias"] == float(np.float32(1 - 0.95 ** bias_step))
+
+
 def _fake_state(opt, p):
     n = p.numel()
     opt.state[p] = {
