@@ -283,18 +283,22 @@ def moment_digests(opt, params) -> dict:
     return {k: v.hex() for k, v in d.items()}
 
 
-def mixed_fixture(ref, name: str, m2_scheme: str, eden: bool, seed, steps: int = 6):
-    """FP32 first moments next to a 4-bit second moment (the reference
-    resolves each moment's scheme on its own, adamw.py:510-521)."""
+def mixed_fixture(ref, name: str, m2_scheme: str, eden: bool, seed, steps: int = 6,
+                  m1_scheme: str = "fp32"):
+    """A scheme pair through QuantizedAdamW: FP32 first moments next to a
+    4-bit second moment (the reference resolves each moment's scheme on its
+    own, adamw.py:510-521), or a 4-bit m1 next to one of the fp32-read m2
+    schemes whose storage bias is c_t or c_{t+1} (adamw.py:112-116, 655-683;
+    quantization.py:581-582)."""
     shapes = [(64, 512), (768,), (32, 128)]
     params = [torch.nn.Parameter(S.init_param(s, i, torch.float32, "cpu"))
               for i, s in enumerate(shapes)]
     kw = dict(lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1,
-              m1_quant_scheme="fp32", m2_quant_scheme=m2_scheme, use_eden_m2=eden)
+              m1_quant_scheme=m1_scheme, m2_quant_scheme=m2_scheme, use_eden_m2=eden)
     if seed is not None:
         kw["quant_rng_seed"] = seed
     opt = ref.QuantizedAdamW(params, **kw)
-    meta = {"name": name, "shapes": [list(s) for s in shapes], "m1_scheme": "fp32",
+    meta = {"name": name, "shapes": [list(s) for s in shapes], "m1_scheme": m1_scheme,
             "m2_scheme": m2_scheme, "eden": eden, "quant_rng_seed": seed, "steps": steps,
             "grad_std": 1e-3, "per_step": []}
     arrays = {}
@@ -327,6 +331,13 @@ def main() -> None:
         if item == "mixed":
             mixed_fixture(ref, "fp32m1_zipsr", "dyn4_upd_sr_fp32read", False, 11)
             mixed_fixture(ref, "fp32m1_zeeden", "dyn4_nz", True, None)
+        elif item == "schemes":
+            mixed_fixture(ref, "fp32m1_lookahead", "dyn4_lookahead_sr", False, 23)
+            mixed_fixture(ref, "nf4_lookahead", "dyn4_lookahead_sr", False, 21, m1_scheme="nf4")
+            mixed_fixture(ref, "nf4_nextbc", "dyn4_upd_sr_fp32read_nextbc", False, 22,
+                          m1_scheme="nf4")
+            mixed_fixture(ref, "nf4_lin4_fp32read", "lin4_upd_sr_fp32read", False, 24,
+                          m1_scheme="nf4")
         elif item == "ckpt":
             checkpoint_fixture(ref, "zeeden", "ze-eden", None)
             checkpoint_fixture(ref, "zipsr", "zip-sr", 4321)

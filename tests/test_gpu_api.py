@@ -427,12 +427,16 @@ def test_fp32_m1_first_step_matches_adamw_and_stores_quantized_m2(scheme):
     assert saved.shape == p_q.shape and torch.isfinite(saved).all()
 
 
-@pytest.mark.parametrize("name", ["fp32m1_zipsr", "fp32m1_zeeden"])
-def test_fp32_m1_with_4bit_m2_matches_reference_trajectory(name):
-    """An FP32 m1 next to a 4-bit m2 (the reference resolves each moment's
-    scheme on its own, adamw.py:510-521), 6 steps: the FP32 moments, the m2
-    codes and scales bit-exact with the reference's own run (its draws for
-    the SR scheme), parameters within rtol 1e-6."""
+@pytest.mark.parametrize("name", ["fp32m1_zipsr", "fp32m1_zeeden", "fp32m1_lookahead",
+                                  "nf4_lookahead", "nf4_nextbc", "nf4_lin4_fp32read"])
+def test_scheme_pair_matches_reference_trajectory(name):
+    """Scheme pairs through QuantizedAdamW, 6 steps against the reference's own
+    run (its draws for the SR schemes): an FP32 m1 next to a 4-bit m2 (the
+    reference resolves each moment's scheme on its own, adamw.py:510-521), and
+    an nf4 m1 next to the fp32-read update-SR m2 schemes, whose storage bias is
+    the next step's c_{t+1} (dyn4_lookahead_sr, dyn4_upd_sr_fp32read_nextbc)
+    or c_t (lin4_upd_sr_fp32read; adamw.py:112-116, 655-683).  Codes, scales
+    and FP32 moments bit-exact, parameters within rtol 1e-6."""
     import hashlib
     import json
     import os
@@ -444,8 +448,9 @@ def test_fp32_m1_with_4bit_m2_matches_reference_trajectory(name):
     arrays = dict(np.load(os.path.join(golden, f"mixed_{name}.npz")))
     shapes = [tuple(s) for s in meta["shapes"]]
     params = [torch.nn.Parameter(S.init_param(s, i, torch.float32, DEV)) for i, s in enumerate(shapes)]
-    kw = dict(lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1, m1_quant_scheme="fp32",
-              m2_quant_scheme=meta["m2_scheme"], use_eden_m2=meta["eden"])
+    kw = dict(lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1,
+              m1_quant_scheme=meta["m1_scheme"], m2_quant_scheme=meta["m2_scheme"],
+              use_eden_m2=meta["eden"])
     seed = meta["quant_rng_seed"]
     if seed is not None:
         kw["quant_rng_seed"] = seed
