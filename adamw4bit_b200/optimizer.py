@@ -430,8 +430,10 @@ class QuantizedAdamW(Optimizer):
 
 
 class AdamW8bit(QuantizedAdamW):
-    """Compatibility name of the reference (adamw.py:865-866); its 8-bit
-    defaults are outside this package, so 4-bit schemes must be given."""
+    """The reference's compatibility name (adamw.py:865-866), kept so imports
+    resolve.  8-bit schemes are not supported by this package: constructed
+    with its 8-bit defaults it raises NotImplementedError, and it steps only
+    when 4-bit schemes are given explicitly."""
 
 
 class ZIPSRAdamW4Bit(QuantizedAdamW):
