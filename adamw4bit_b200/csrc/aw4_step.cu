@@ -225,7 +225,7 @@ step_kernel(const __grid_constant__ StepLaunch L) {
         const int tile0 = (tile - D.tile_begin) * kStepBlocksPerTile;
         // ZeRO-2: each sub-block's gradient sums are requested from the
         // switch one sub-block ahead, so their round trip overlaps the math
-        uint32_t gnext[8];
+        uint32_t gnext[8] = {0, 0, 0, 0, 0, 0, 0, 0};   // stays 0 past the tensor end
         if constexpr (GMC) {
             const int blk = tile0 + 8 * warp + h;
             if (blk < D.nblocks) issue8_reduce<GT>(D.grad, (int64_t)blk * kBlock + 8 * g.j, gnext);
@@ -247,7 +247,10 @@ step_kernel(const __grid_constant__ StepLaunch L) {
             float p[8], gr[8], m1[8], m2[8];
             uint32_t w1 = 0, w2 = 0;
             float s1 = 0.0f, s2 = 0.0f;
-            if (active) {
+            {
+                // an inactive group reads the tensor's last block (never stored)
+                const int blk = min(tile0 + slot, D.nblocks - 1);
+                const int64_t e0 = (int64_t)blk * kBlock + 8 * g.j;
                 Elem<PT>::load8(D.param, e0, p);
                 if constexpr (GMC) {   // grad is a multicast address: the sum over ranks
                     finish8_reduce<GT>(gcur, gr);
@@ -264,13 +267,6 @@ step_kernel(const __grid_constant__ StepLaunch L) {
                     w2 = __ldcs(reinterpret_cast<const unsigned int*>(D.c2 + (e0 >> 1)));
                     s1 = __ldcs(D.s1 + blk);
                     s2 = __ldcs(D.s2 + blk);
-                }
-            } else {
-#pragma unroll
-                for (int i = 0; i < 8; ++i) p[i] = gr[i] = 0.0f;
-                if constexpr (F1) {
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) m1[i] = 0.0f;
                 }
             }
             // Packed f32x2 arithmetic throughout: multiplies, FMAs, and
@@ -294,14 +290,22 @@ step_kernel(const __grid_constant__ StepLaunch L) {
             const float sc1 = F1 ? 0.0f : max_nan(group_max16(amax1), kScaleFloor);
             const float gmax2 = group_max16(amax2);
             const float sc2 = max_nan(gmax2, kScaleFloor);
-            bool ok = active && amax1 <= H.m1_fast_max && amax2 <= H.m2_fast_max &&
+            const bool lane_ok = active && amax1 <= H.m1_fast_max && amax2 <= H.m2_fast_max &&
                       sc1 <= kMarksteinMaxDivisor && sc2 <= kMarksteinMaxDivisor &&
                       (gmax2 >= kScaleFloor || !L.eden);
-            ok = none_tiny_warp(nt, ok);
-            if (M1 == AW4_SR_VALUE) ok = none_tiny_warp(m1, ok);
-            if (M2 != AW4_RTN || L.eden) ok = none_tiny_warp(m2, ok);
+            const bool chk2 = M2 != AW4_RTN || L.eden;
+            float mn = lane_absmin(nt);
+            if (M1 == AW4_SR_VALUE) mn = fminf(mn, lane_absmin(m1));
+            if (chk2) mn = fminf(mn, lane_absmin(m2));
+            bool all = __all_sync(0xffffffffu, lane_ok && mn >= kMarksteinMinNumerator);
+            if (!all) {   // a zero or a tiny value somewhere: the exact per-value tests
+                bool ok = lane_ok && !any_tiny(nt);
+                if (M1 == AW4_SR_VALUE) ok = ok && !any_tiny(m1);
+                if (chk2) ok = ok && !any_tiny(m2);
+                all = __all_sync(0xffffffffu, ok);
+            }
             float u[8];
-            if (__all_sync(0xffffffffu, ok)) {
+            if (all) {
                 update_fast(q, m1, m2, H, one);
                 vmuls8(p, p, H.decay);               // p.mul_(1 - lr*wd)
 #pragma unroll
@@ -317,7 +321,7 @@ step_kernel(const __grid_constant__ StepLaunch L) {
                         encode_fast<M2>(sm.s2, r2, g, m2, sc2, u, zf2, L.eden, H.sr_bias, H.eps,
                                         H.sr_rbias, one, &ns2);
                     __stcs(reinterpret_cast<unsigned int*>(D.c2 + (e0 >> 1)), c2);
-                    if (g.j == 0) sm.scales[1][slot] = ns2;
+                    sm.scales[1][slot] = ns2;   // the same value from every lane of the group
                 } else {
                     if (M1 == AW4_SR_VALUE) load_uniforms<M1>(u, D.d1, H.m1_key, H, D, e0, true);
                     float ns1, ns2;
@@ -330,10 +334,8 @@ step_kernel(const __grid_constant__ StepLaunch L) {
                                         H.sr_rbias, one, &ns2);
                     __stcs(reinterpret_cast<unsigned int*>(D.c1 + (e0 >> 1)), c1);
                     __stcs(reinterpret_cast<unsigned int*>(D.c2 + (e0 >> 1)), c2);
-                    if (g.j == 0) {
-                        sm.scales[0][slot] = ns1;
-                        sm.scales[1][slot] = ns2;
-                    }
+                    sm.scales[0][slot] = ns1;   // the same value from every lane of the group
+                    sm.scales[1][slot] = ns2;
                 }
                 continue;
             }
