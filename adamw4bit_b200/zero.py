@@ -320,7 +320,18 @@ class ZeRO1AdamW4Bit:
                 p.grad.zero_()
 
     @torch.no_grad()
-    def step(self) -> None:
+    def step(self, round_begin=None, round_end=None) -> None:
+        """One optimizer step: per gather round, one fused update launch over
+        this rank's owned segments (then that round's gather), then the
+        FP32-state tensors.
+
+        round_begin(r) / round_end(r), when given, are called on the host just
+        before and just after round r's update launch is enqueued on the
+        current stream.  A caller that streams gradients in and the model out
+        per round orders its copies there: round r reads the gradients of
+        ``segments[r]`` and writes this rank's values ``owned[r]`` of the flat
+        model, so the next round's gradients can upload while round r
+        updates, and round r's values can download while round r+1 updates."""
         if self.grad_reduce == "multicast" and any(
                 p.grad is None or p.grad.data_ptr() != ptr
                 for p, ptr in zip(self.all_params, self.grad_ptrs)):
@@ -373,6 +384,8 @@ class ZeRO1AdamW4Bit:
                     # Philox ordinal: the position among all parameters, as in
                     # the single-GPU optimizer, so SR draws do not depend on sharding
                     None, None, n, s, self.qindex[ti], 0, copy, multicast, int(reduce_mc)))
+            if round_begin is not None:
+                round_begin(r)
             if descs:
                 arr = (N.QTensor * len(descs))(*descs)
                 if self.launch_timings is not None:
@@ -386,6 +399,8 @@ class ZeRO1AdamW4Bit:
                 if self.launch_timings is not None:
                     e1.record(cur)
                     self.launch_timings.append((e0, e1, sum(d.numel for d in descs), pdt, gdt))
+            if round_end is not None:
+                round_end(r)
             if W > 1 and self.gather_mode == "nccl":
                 base = r * W * self.chunk
                 region = self.flat[base:base + W * self.chunk]

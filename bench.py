@@ -456,7 +456,7 @@ def run_ours(args, rank, world, local):
                                   param_dtype=torch.bfloat16 if master else torch.float32)
     # FP32 masters (sharded over the ranks at N>1) and the BF16 model copy
     # written by the update kernel; at N>1 the model is all-gathered
-    opt = ZeRO1AdamW4Bit(params, recipe=args.recipe, rounds=args.rounds if world > 1 else 1,
+    opt = ZeRO1AdamW4Bit(params, recipe=args.recipe, rounds=args.rounds,
                          master_weights=master, reserve_sms=args.reserve_sms,
                          gather="multicast" if args.gather == "multicast" else "nccl",
                          grad_reduce=args.grad_reduce, quant_rng_seed=1234)
@@ -586,44 +586,86 @@ def run_e2e(args, opt, dev, world, total):
     its gradients from pinned host memory (its owned segments; with the
     ZeRO-2 reduction, its full local gradients), steps, and copies its updated
     BF16 model shard back to pinned host memory, all inside the timed region.
-    The read-back of step t runs on a second stream and overlaps the upload of
-    step t+1's gradients (PCIe carries both directions at once); step t+1's
-    update waits for that read-back before it overwrites the model, and the
-    timed region ends after the last read-back.  Afterwards a strided sample
-    of the host copy is compared with the device model."""
-    segs = [seg for round_segs in opt.segments for seg in round_segs]
-    if opt.grad_reduce == "multicast":
-        segs = [(ti, 0, p.numel(), 0) for ti, p in enumerate(opt.params)]
-    host_g = [opt.params[ti].grad.reshape(-1)[s:s + n].to("cpu").pin_memory()
-              for ti, s, n, _ in segs]
+
+    The copies are pipelined per round of the step (ZeRO1AdamW4Bit.step's
+    round hooks): gradients upload on a copy stream, round after round, each
+    round once the previous step's update has consumed that round's
+    gradients; round r's update waits for its upload and for the previous
+    step's read-back of its model values; round r's values download on a
+    second stream while round r+1 updates.  PCIe then carries both directions
+    at once and the updates hide under the copies.  With the ZeRO-2 reduction
+    every rank's full gradients must be in place before any rank's first
+    round, so there the upload precedes the step.  The timed region ends
+    after the last read-back; afterwards a strided sample of the host copy is
+    compared with the device model."""
+    cur = torch.cuda.current_stream(dev)
+    up = torch.cuda.Stream(dev)
+    side = torch.cuda.Stream(dev)
+    R = len(opt.segments)
+    zero2 = opt.grad_reduce == "multicast"
+    if zero2:
+        seg_rounds = [[(ti, 0, p.numel(), 0) for ti, p in enumerate(opt.params)]]
+    else:
+        seg_rounds = [list(opt.segments[r]) for r in range(R)]
+    host_g = [[opt.params[ti].grad.reshape(-1)[s:s + n].to("cpu").pin_memory()
+               for ti, s, n, _ in segs] for segs in seg_rounds]
     small = [opt.all_params[i] for i in opt.sindex]
     host_gs = [p.grad.to("cpu").pin_memory() for p in small]
-    owned = [(a, b) for a, b in opt.owned if b > a]
-    host_p = [torch.empty(b - a, dtype=opt.flat.dtype, pin_memory=True) for a, b in owned]
-    h2d = sum(h.numel() * h.element_size() for h in host_g + host_gs)
-    d2h = sum(h.numel() * h.element_size() for h in host_p)
-    cur = torch.cuda.current_stream(dev)
-    side = torch.cuda.Stream(dev)
-    read_back = torch.cuda.Event()
-    read_back.record(side)          # created and complete: nothing to wait for yet
+    owned = list(opt.owned)
+    host_p = [torch.empty(b - a, dtype=opt.flat.dtype, pin_memory=True) if b > a else None
+              for a, b in owned]
+    h2d = sum(h.numel() * h.element_size() for hs in host_g for h in hs)
+    h2d += sum(h.numel() * h.element_size() for h in host_gs)
+    d2h = sum(h.numel() * h.element_size() for h in host_p if h is not None)
+
+    def ev():
+        e = torch.cuda.Event()
+        e.record(cur)   # complete: nothing to wait for yet
+        return e
+    consumed = [ev() for _ in seg_rounds]   # the update has read these gradients
+    read_back = [ev() for _ in owned]       # these model values are on the host
+    stepped = ev()
+    uploaded = [torch.cuda.Event() for _ in seg_rounds]
+    small_up = torch.cuda.Event()
 
     def one():
-        for (ti, s, n, _), hg in zip(segs, host_g):
-            opt.params[ti].grad.reshape(-1)[s:s + n].copy_(hg, non_blocking=True)
-        for p, hg in zip(small, host_gs):
-            p.grad.copy_(hg, non_blocking=True)
-        cur.wait_event(read_back)   # the previous step's model is on the host
-        opt.step()
-        stepped = torch.cuda.Event()
+        with torch.cuda.stream(up):
+            if zero2:   # other ranks read these gradients until the step ends
+                up.wait_event(stepped)
+            for r, (segs, hs) in enumerate(zip(seg_rounds, host_g)):
+                up.wait_event(consumed[r])
+                for (ti, s, n, _), hg in zip(segs, hs):
+                    opt.params[ti].grad.reshape(-1)[s:s + n].copy_(hg, non_blocking=True)
+                uploaded[r].record(up)
+            up.wait_event(stepped)          # the FP32-state tensors read theirs last
+            for p, hg in zip(small, host_gs):
+                p.grad.copy_(hg, non_blocking=True)
+            small_up.record(up)
+
+        def begin(r):
+            cur.wait_event(uploaded[0] if zero2 else uploaded[r])
+            cur.wait_event(read_back[r])
+
+        def end(r):
+            consumed[0 if zero2 else r].record(cur)
+            side.wait_event(consumed[0 if zero2 else r])
+            (a, b), hp = owned[r], host_p[r]
+            if hp is not None:
+                with torch.cuda.stream(side):
+                    hp.copy_(opt.flat[a:b], non_blocking=True)
+            read_back[r].record(side)
+            if r == R - 1:   # the FP32-state update follows the last round
+                cur.wait_event(small_up)
+
+        if zero2:   # every rank's gradients in place before the step's first round
+            cur.wait_event(uploaded[0])
+            cur.wait_event(small_up)
+        opt.step(round_begin=begin, round_end=end)
         stepped.record(cur)
-        side.wait_event(stepped)
-        with torch.cuda.stream(side):
-            for (a, b), hp in zip(owned, host_p):
-                hp.copy_(opt.flat[a:b], non_blocking=True)
-        read_back.record(side)
 
     one()
-    cur.wait_stream(side)           # the timed region starts with an idle side stream
+    cur.wait_stream(side)           # the timed region starts with idle copy streams
+    cur.wait_stream(up)
     barrier(world)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
@@ -631,11 +673,14 @@ def run_e2e(args, opt, dev, world, total):
     for _ in range(args.e2e_steps):
         one()
     cur.wait_stream(side)           # the last read-back is inside the timed region
+    cur.wait_stream(up)
     e1.record(cur)
     barrier(world)
     ms = max_over_ranks(e0.elapsed_time(e1), world)
     torch.cuda.synchronize()
     for (a, b), hp in zip(owned, host_p):
+        if hp is None:
+            continue
         stride = max(1, (b - a) // 4099)
         if not torch.equal(hp[::stride].to(dev), opt.flat[a:b][::stride]):
             raise RuntimeError("e2e: the host copy does not hold the stepped model")
@@ -643,7 +688,8 @@ def run_e2e(args, opt, dev, world, total):
     return {"value": total * args.e2e_steps / (ms / 1e3), "unit": UNIT,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
             "bytes_are_per_rank": world > 1, "ms_per_step": ms / args.e2e_steps,
-            "steps": args.e2e_steps, "readback_checked": True}
+            "steps": args.e2e_steps, "pipelined_rounds": 1 if zero2 else R,
+            "readback_checked": True}
 
 
 def main():
@@ -654,7 +700,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference", "reference-gpu", "reference-gpu-eager",
                                        "reference-cpu", "reference-cpu-eager"],
                     default="ours")
-    ap.add_argument("--rounds", type=int, default=4, help="ZeRO-1 gather rounds")
+    ap.add_argument("--rounds", type=int, default=4,
+                    help="rounds per step: one update launch each (and, at N>1, one gather)")
     ap.add_argument("--recipe", choices=["ze-eden", "zip-sr"], default="ze-eden",
                     help="the optimizer recipe (BASELINE config 5 is ZE-EDEN)")
     ap.add_argument("--grad-reduce", choices=["local", "multicast"], default="local",
@@ -667,7 +714,7 @@ def main():
                          "replica by the update kernel through NVSwitch multicast, or "
                          "all-gathered by NCCL (bf16, default), or the FP32 parameters "
                          "all-gathered by NCCL")
-    ap.add_argument("--e2e-steps", type=int, default=4)
+    ap.add_argument("--e2e-steps", type=int, default=8)
     ap.add_argument("--no-legs", dest="legs", action="store_false",
                     help="N=1: skip the drop-in and ZIP-SR legs")
     ap.add_argument("--cpu-sample", type=int, default=1 << 27,
