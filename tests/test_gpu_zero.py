@@ -169,6 +169,72 @@ def test_zero1_master_weights_on_one_gpu_matches_fp32_step():
             assert torch.equal(opt.master[so:so + n].view(torch.int32), want.view(torch.int32))
 
 
+def test_round_hooks_stream_gradients_in_and_model_out_per_round():
+    """step(round_begin, round_end) on one rank: the hooks run once per round
+    in order, and gradients uploaded from pinned host memory round by round
+    on a copy stream, with each round's BF16 values downloaded on another
+    stream while the next round updates, give the plain step's model and
+    masters bit for bit."""
+    from adamw4bit_b200.zero import ZeRO1AdamW4Bit
+    dev = torch.device("cuda", 0)
+    vals, grads = _make(dev, seed=5)
+
+    def build():
+        model = [torch.nn.Parameter(v.to(torch.bfloat16)) for v in vals]
+        return model, ZeRO1AdamW4Bit(model, recipe="zip-sr", rounds=3, master_weights=True,
+                                     quant_rng_seed=9)
+
+    plain_model, plain = build()
+    _run(plain, plain_model, grads)
+    model, opt = build()
+    for p, g in zip(model, grads[0]):
+        p.grad = torch.zeros_like(g)
+    cur = torch.cuda.current_stream(dev)
+    up, down = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    R = len(opt.segments)
+    calls, host_models = [], []
+    for step_grads in grads:
+        host = [g.cpu().pin_memory() for g in step_grads]
+        for i in opt.sindex:
+            opt.all_params[i].grad.copy_(host[i], non_blocking=True)
+        uploaded = []
+        with torch.cuda.stream(up):
+            up.wait_stream(cur)
+            for r in range(R):
+                for ti, s, n, _ in opt.segments[r]:
+                    q = opt.qindex[ti]
+                    opt.params[ti].grad.reshape(-1)[s:s + n].copy_(
+                        host[q].reshape(-1)[s:s + n], non_blocking=True)
+                e = torch.cuda.Event()
+                e.record(up)
+                uploaded.append(e)
+        out = [torch.empty(b - a, dtype=torch.bfloat16, pin_memory=True) for a, b in opt.owned]
+
+        def begin(r):
+            calls.append(("begin", r))
+            cur.wait_event(uploaded[r])
+
+        def end(r):
+            calls.append(("end", r))
+            done = torch.cuda.Event()
+            done.record(cur)
+            down.wait_event(done)
+            a, b = opt.owned[r]
+            with torch.cuda.stream(down):
+                out[r].copy_(opt.flat[a:b], non_blocking=True)
+
+        opt.step(round_begin=begin, round_end=end)
+        cur.wait_stream(down)
+        host_models.append(out)
+    torch.cuda.synchronize()
+    assert calls == [(k, r) for _ in grads for r in range(R) for k in ("begin", "end")]
+    for a, b in zip(model, plain_model):
+        assert torch.equal(a.detach().view(torch.int16), b.detach().view(torch.int16))
+    assert torch.equal(opt.master.view(torch.int32), plain.master.view(torch.int32))
+    for (a, b), h in zip(opt.owned, host_models[-1]):
+        assert torch.equal(h.view(torch.int16), plain.flat[a:b].cpu().view(torch.int16))
+
+
 def _run(opt, params, grads):
     for step_grads in grads:
         for p, g in zip(params, step_grads):
