@@ -553,19 +553,26 @@ def run_ours(args, rank, world, local):
         if world > 1:
             line["ranks"] = ranks
             # every GPU receives the whole model minus its own shard each step
-            nv = (world - 1) / world * total * (2 if master else 4)
+            # (NCCL); a multimem store goes through the switch to every
+            # replica, this rank's own included, so the multicast gather
+            # brings the whole model in
+            share = 1.0 if args.gather == "multicast" else (world - 1) / world
+            nv = share * total * (2 if master else 4)
             line["gather"] = {"ingress_bytes_per_gpu": nv,
                               "ingress_gbs": round(nv / (ms_per_step / 1e3) / 1e9, 1),
                               "peak_gbs": 770.0,
                               "peak_source": "measured peer copy, per direction",
                               "floor_ms": round(nv / 770e9 * 1e3, 2)}
         if zero2:
-            # per GPU and step, each NVLink direction carries 2 B per value:
-            # out, its gradients to the switch's reductions of every shard
-            # ((W-1)/W) and its shard's multicast model stores (1/W); in, the
-            # reduced sums of its shard (1/W) and the other shards' model
-            # values ((W-1)/W)
-            nv = 2.0 * total
+            # per GPU and step, each NVLink direction carries 2 (1 + 1/W) B
+            # per value (BF16 gradients and model).  Out: the switch reads
+            # every rank's copy of a shard for its owner's ld_reduce, this
+            # rank's own copy included, so all of its local gradients (2 B),
+            # plus its shard's multicast model stores (2/W).  In: its shard's
+            # reduced sums (2/W) and every shard of the model, its own
+            # included (2).  Measured with ld_reduce alone (BF16, 2 and 4
+            # GPUs): each GPU's egress is its whole buffer, at 670-708 GB/s.
+            nv = 2.0 * total * (1.0 + 1.0 / world)
             line["nvlink"] = {"bytes_per_direction_per_gpu": nv,
                               "achieved_gbs": round(nv / (ms_per_step / 1e3) / 1e9, 1),
                               "peak_gbs": 770.0, "peak_source": "measured peer copy, per direction",
