@@ -279,6 +279,19 @@ def run_reference_torch(args, rank, device: str, eager: bool):
         shapes = [(args.values,)]
     total = sum(int(torch.Size(s).numel()) for s in shapes)
     params, grads = make_workload(dev, shapes)
+    compat = None
+    if args.compile_compat and not eager:
+        # the reference passes torch.compile(isolate_recompiles=True)
+        # (_optimized.py:244-246), a keyword this torch lacks; dropping it
+        # keeps every other argument and the reference's code unchanged
+        orig_compile = torch.compile
+
+        def compile_without_isolation(*a, **kw):
+            kw.pop("isolate_recompiles", None)
+            return orig_compile(*a, **kw)
+        torch.compile = compile_without_isolation
+        compat = "torch.compile called without isolate_recompiles (absent from torch " \
+                 f"{torch.__version__})"
     opt = RefZE(params, lr=1e-3, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1,
                 optimized=not eager)
     for p_, g_ in zip(params, grads):
@@ -319,7 +332,8 @@ def run_reference_torch(args, rank, device: str, eager: bool):
                       "config": {"workload": WORKLOAD if device == "cuda" else
                                  "4096x4096 FP32 param, BF16 grads, ZE-EDEN",
                                  "values": total, "tensors": len(shapes)},
-                      "warmup_seconds": warm_s, **extra}), flush=True)
+                      "warmup_seconds": warm_s, **({"compat": compat} if compat else {}),
+                      **extra}), flush=True)
 
 
 def reference_cpu_rates(steps: int) -> dict:
@@ -728,6 +742,10 @@ def main():
                          "up, bf16 below (multicast falls back to NCCL where the "
                          "platform has none)")
     ap.add_argument("--e2e-steps", type=int, default=8)
+    ap.add_argument("--compile-compat", action="store_true",
+                    help="--impl reference-gpu/-cpu: let the reference's optimized path "
+                         "run on this torch by dropping the isolate_recompiles keyword "
+                         "it passes to torch.compile")
     ap.add_argument("--no-legs", dest="legs", action="store_false",
                     help="N=1: skip the drop-in and ZIP-SR legs")
     ap.add_argument("--cpu-sample", type=int, default=1 << 27,
