@@ -329,7 +329,9 @@ def run_reference_torch(args, rank, device: str, eager: bool):
                       "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
                       "higher_is_better": True, "impl": impl, "dtype": "f32",
                       "data": "synthetic",
-                      "config": {"workload": WORKLOAD if device == "cuda" else
+                      "config": {"workload": "llama3-8b, FP32 params updated in place, BF16 "
+                                             "grads, ZE-EDEN (BASELINE config 5 through the "
+                                             "reference's API)" if device == "cuda" else
                                  "4096x4096 FP32 param, BF16 grads, ZE-EDEN",
                                  "values": total, "tensors": len(shapes)},
                       "warmup_seconds": warm_s, **({"compat": compat} if compat else {}),
