@@ -166,6 +166,35 @@ def dist_setup(n_gpus: int):
     return rank, world, local
 
 
+def resolve_gather(gather: str, world: int) -> str:
+    """--gather auto: NVSwitch multicast stores from 4 ranks up (measured
+    faster than NCCL's gather there), NCCL's BF16 gather below."""
+    if gather != "auto":
+        return gather
+    return "multicast" if world >= 4 else "bf16"
+
+
+def gather_ingress_bytes(world: int, total: int, master: bool, multicast: bool) -> float:
+    """Model bytes each GPU receives per step.  NCCL's all-gather brings the
+    other ranks' shards, (W-1)/W of the model.  A multimem store goes through
+    the switch to every replica, this rank's own included, so the multicast
+    gather brings the whole model in."""
+    share = 1.0 if multicast else (world - 1) / world
+    return share * total * (2 if master else 4)
+
+
+def zero2_nvlink_bytes(world: int, total: int) -> float:
+    """Bytes per NVLink direction per GPU and step of the fused ZeRO-2 step
+    (BF16 gradients and model): 2 (1 + 1/W) per value.  Out: the switch
+    reads every rank's copy of a shard for its owner's ld_reduce, this rank's
+    own copy included, so all of its local gradients (2 B), plus its shard's
+    multicast model stores (2/W).  In: its shard's reduced sums (2/W) and
+    every shard of the model, its own included (2).  Measured with ld_reduce
+    alone (BF16, 2 and 4 GPUs): each GPU's egress is its whole buffer, at
+    670-708 GB/s."""
+    return 2.0 * total * (1.0 + 1.0 / world)
+
+
 def max_over_ranks(x: float, world: int) -> float:
     if world == 1:
         return x
@@ -467,10 +496,7 @@ def run_ours(args, rank, world, local):
     if args.values:
         shapes = [(args.values,)]   # single-tensor case (profiling)
     total = sum(int(torch.Size(s).numel()) for s in shapes)
-    if args.gather == "auto":
-        # NVSwitch multicast writes each shard to every replica during the
-        # update; measured faster than NCCL's gather from 4 ranks up
-        args.gather = "multicast" if world >= 4 else "bf16"
+    args.gather = resolve_gather(args.gather, world)
     master = args.gather != "fp32"
     params, grads = make_workload(dev, shapes,
                                   param_dtype=torch.bfloat16 if master else torch.float32)
@@ -572,27 +598,14 @@ def run_ours(args, rank, world, local):
                 "e2e": e2e}
         if world > 1:
             line["ranks"] = ranks
-            # every GPU receives the whole model minus its own shard each step
-            # (NCCL); a multimem store goes through the switch to every
-            # replica, this rank's own included, so the multicast gather
-            # brings the whole model in
-            share = 1.0 if gather_mode == "multicast" else (world - 1) / world
-            nv = share * total * (2 if master else 4)
+            nv = gather_ingress_bytes(world, total, master, gather_mode == "multicast")
             line["gather"] = {"ingress_bytes_per_gpu": nv,
                               "ingress_gbs": round(nv / (ms_per_step / 1e3) / 1e9, 1),
                               "peak_gbs": 770.0,
                               "peak_source": "measured peer copy, per direction",
                               "floor_ms": round(nv / 770e9 * 1e3, 2)}
         if zero2:
-            # per GPU and step, each NVLink direction carries 2 (1 + 1/W) B
-            # per value (BF16 gradients and model).  Out: the switch reads
-            # every rank's copy of a shard for its owner's ld_reduce, this
-            # rank's own copy included, so all of its local gradients (2 B),
-            # plus its shard's multicast model stores (2/W).  In: its shard's
-            # reduced sums (2/W) and every shard of the model, its own
-            # included (2).  Measured with ld_reduce alone (BF16, 2 and 4
-            # GPUs): each GPU's egress is its whole buffer, at 670-708 GB/s.
-            nv = 2.0 * total * (1.0 + 1.0 / world)
+            nv = zero2_nvlink_bytes(world, total)
             line["nvlink"] = {"bytes_per_direction_per_gpu": nv,
                               "achieved_gbs": round(nv / (ms_per_step / 1e3) / 1e9, 1),
                               "peak_gbs": 770.0, "peak_source": "measured peer copy, per direction",

@@ -55,3 +55,18 @@ def test_algorithmic_bytes_per_value():
     assert bench.bytes_per_value(4, 2, True) == bench.B_PER_ELEM == 14.125   # bench value
     assert len(bench.llama_1b_shapes()) == 147
     assert sum(int(torch.Size(s).numel()) for s in bench.llama_1b_shapes()) == 852_559_872
+
+
+def test_multi_gpu_nvlink_accounting():
+    """NVLink bytes per GPU and step for config 5 (8.03 G values): NCCL's
+    gather brings (W-1)/W of the BF16 model, the multicast stores the whole
+    model (the switch delivers a rank's own shard back to it), and the fused
+    ZeRO-2 step moves 2 (1 + 1/W) B per value each way; --gather auto picks
+    multicast from 4 ranks up."""
+    n = 8_030_261_248
+    assert bench.gather_ingress_bytes(8, n, True, False) == 7 / 8 * n * 2
+    assert bench.gather_ingress_bytes(8, n, True, True) == n * 2
+    assert bench.gather_ingress_bytes(2, n, False, False) == n * 2      # FP32, half the model
+    assert round(bench.zero2_nvlink_bytes(2, n) / 1e9, 2) == 24.09
+    assert [bench.resolve_gather("auto", w) for w in (2, 4, 8)] == ["bf16", "multicast", "multicast"]
+    assert bench.resolve_gather("bf16", 8) == "bf16"
