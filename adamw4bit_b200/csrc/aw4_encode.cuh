@@ -292,9 +292,10 @@ __device__ __forceinline__ uint32_t encode_fast_upd_sr(const SchemeRegs& R, cons
     const float ys = rcp_nr(sc);
     const f2 nsc = pk2(-sc, -sc), yss = pk2(ys, ys), scp = pk2(sc, sc);
     const f2 rb = pk2(rbias, rbias), nb = pk2(-bias, -bias);
-    const f2 hh = pk2(0.5f, 0.5f), s24 = pk2(0x1p-24f, 0x1p-24f);
+    const f2 hh = pk2(0.5f, 0.5f);
     const float eps24 = fmul(eps, 0x1p-24f);
-    const f2 ee = pk2(eps24, eps24);
+    const f2 nee = pk2(-eps24, -eps24), ns24 = pk2(-0x1p-24f, -0x1p-24f);
+    const f2 one2 = pk2(g.one, g.one), tiny = pk2(kNrMin, kNrMin);
     uint32_t packed = 0;
 #pragma unroll
     for (int i = 0; i < 8; i += 2) {
@@ -312,19 +313,23 @@ __device__ __forceinline__ uint32_t encode_fast_upd_sr(const SchemeRegs& R, cons
         const f2 t2 = f2_fma(f2_fma(q0, nb, t1), rb, q0);
         float ta, tb;
         upk2(t2, ta, tb);
-        // sqrt_nr of both
-        const f2 y = pk2(rsqrt_approx(fmaxf(ta, kNrMin)), rsqrt_approx(fmaxf(tb, kNrMin)));
+        // sqrt_nr of both; the approximation reads t + 2^-126, which is t
+        // for every nonzero t (>= 2^-101) and 2^-126 for t == 0
+        float ga, gb;
+        upk2(f2_fma(t2, one2, tiny), ga, gb);
+        const f2 y = pk2(rsqrt_approx(ga), rsqrt_approx(gb));
         const f2 sq = f2_mul(t2, y), h = f2_mul(hh, y);
         float sa, sb;
         upk2(sq, sa, sb);
         const f2 root = f2_fma(pk2(ffma(-sa, sa, ta), ffma(-sb, sb, tb)), h, sq);
-        // rcp_nr of 2^-24 (root + eps), both
-        float da, db;
-        upk2(f2_fma(root, s24, ee), da, db);
-        const float ra = rcp_approx(da), rbb = rcp_approx(db);
+        // rcp_nr of d = 2^-24 (root + eps), both, from nd = -d
+        const f2 nd = f2_fma(root, ns24, nee);
+        float na, nb;
+        upk2(nd, na, nb);
+        const float ra = rcp_approx(-na), rbb = rcp_approx(-nb);
         const f2 yy = pk2(ra, rbb);
         float fa, fb;
-        upk2(f2_fma(pk2(ffma(-da, ra, 1.0f), ffma(-db, rbb, 1.0f)), yy, yy), fa, fb);
+        upk2(f2_fma(f2_fma(nd, yy, one2), yy, yy), fa, fb);
 #pragma unroll
         for (int k = 0; k < 2; ++k) {
             const float4 t = g.sr_tab[idx[k]];
