@@ -285,7 +285,12 @@ step_kernel(const __grid_constant__ StepLaunch L) {
             vmuls8(nt, m1, H.pos_step);
 
             // One warp-uniform decision per sub-block: when every lane meets the
-            // fast preconditions the rest runs without per-lane branches.
+            // fast preconditions the rest runs without per-lane branches.  The
+            // smallest magnitude among the values later divided (nt, and m1 or
+            // m2 where SR or EDEN divides them) settles the tiny-value
+            // precondition with one compare and one vote; only when some lane
+            // holds a zero or a value below 2^-100 do the exact per-value tests
+            // run, and the warp votes again on their result.
             // (an FP32 m1 has no block scale: 0 passes the divisor bound below)
             const float sc1 = F1 ? 0.0f : max_nan(group_max16(amax1), kScaleFloor);
             const float gmax2 = group_max16(amax2);
