@@ -622,25 +622,6 @@ __device__ __forceinline__ float level_of(float cbv, int code) {
     return __shfl_sync(0xffffffffu, cbv, code);
 }
 
-// Decodes 8 packed codes (one 32-bit word, value i in bits 4i..4i+3) to
-// cb[code] * scale.  The shuffle source lane is taken modulo 32, and lanes l
-// and l + 16 hold the same level, so w >> 4i needs no mask.  The product is
-// an FMA with a +0 addend: the same value as the multiply (the scale is >= 0
-// and products cannot be -0 here), and an FMA result cannot be contracted
-// into a following add.
-__device__ __forceinline__ void decode8(float cbv, uint32_t w, float scale, float v[8]) {
-    float lv[8];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) lv[i] = __shfl_sync(0xffffffffu, cbv, (int)(w >> (4 * i)));
-    const unsigned long long ss = pk2(scale, scale), zz = pk2(0.0f, 0.0f);
-#pragma unroll
-    for (int i = 0; i < 8; i += 2) {
-        unsigned long long r;
-        asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(pk2(lv[i], lv[i + 1])), "l"(ss), "l"(zz));
-        upk2(r, v[i], v[i + 1]);
-    }
-}
-
 // Decodes 8 packed codes from the block's scaled codebook: lane 16h + k of
 // the block's 16-lane group holds cbs = RN(cb[k] * scale), and a shuffle
 // confined to the group reads lane `code` (the segment keeps only the low 4
