@@ -208,25 +208,12 @@ __device__ __forceinline__ void vmuls8(float d[8], const float a[8], float s) {
 #pragma unroll
     for (int i = 0; i < 8; i += 2) upk2(f2_mul(pk2(a[i], a[i + 1]), ss), d[i], d[i + 1]);
 }
-// d[i] = fma(a[i], b[i], c[i])
-__device__ __forceinline__ void vfma8(float d[8], const float a[8], const float b[8],
-                                      const float c[8]) {
-#pragma unroll
-    for (int i = 0; i < 8; i += 2)
-        upk2(f2_fma(pk2(a[i], a[i + 1]), pk2(b[i], b[i + 1]), pk2(c[i], c[i + 1])), d[i], d[i + 1]);
-}
 // d[i] = fma(s, a[i], c[i])
 __device__ __forceinline__ void vfmas8(float d[8], float s, const float a[8], const float c[8]) {
     const f2 ss = pk2(s, s);
 #pragma unroll
     for (int i = 0; i < 8; i += 2)
         upk2(f2_fma(ss, pk2(a[i], a[i + 1]), pk2(c[i], c[i + 1])), d[i], d[i + 1]);
-}
-// d[i] = fma(a[i], s, c): scalar multiplier and addend
-__device__ __forceinline__ void vfmass8(float d[8], const float a[8], float s, float c) {
-    const f2 ss = pk2(s, s), cc = pk2(c, c);
-#pragma unroll
-    for (int i = 0; i < 8; i += 2) upk2(f2_fma(pk2(a[i], a[i + 1]), ss, cc), d[i], d[i + 1]);
 }
 // d[i] = RN(a[i] + b[i]), with one == 1.0 at run time
 __device__ __forceinline__ void vadd8(float d[8], const float a[8], const float b[8], float one) {
