@@ -732,14 +732,111 @@ def run_e2e(args, opt, dev, world, total):
             "readback_checked": True}
 
 
+def probe_pcie(args) -> None:
+    """Pinned host <-> device copy rates of the GPU box (the floor of `e2e`):
+    one 4 GB BF16 buffer each way, upload alone, download alone and both at
+    once on two streams; best of 3, GB/s per direction."""
+    dev = torch.device("cuda", 0)
+    n = (4 << 30) // 2
+    hg = torch.empty(n, dtype=torch.bfloat16).pin_memory()
+    hp = torch.empty(n, dtype=torch.bfloat16).pin_memory()
+    hg.fill_(1.0)
+    dg = torch.empty(n, dtype=torch.bfloat16, device=dev)
+    dp = torch.ones(n, dtype=torch.bfloat16, device=dev)
+    s1, s2 = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    out = {"probe": "pcie", "bytes_per_direction": 2 * n}
+    for name, up, down in (("h2d_gbs", True, False), ("d2h_gbs", False, True),
+                           ("both_gbs_each_way", True, True)):
+        best = 0.0
+        for _ in range(3):
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            if up:
+                with torch.cuda.stream(s1):
+                    dg.copy_(hg, non_blocking=True)
+            if down:
+                with torch.cuda.stream(s2):
+                    hp.copy_(dp, non_blocking=True)
+            torch.cuda.synchronize()
+            best = max(best, 2 * n / (time.perf_counter() - t0) / 1e9)
+        out[name] = round(best, 1)
+    print(json.dumps(out), flush=True)
+
+
+def probe_ld_reduce(args, rank: int, world: int, local: int) -> None:
+    """multimem.ld_reduce through NVSwitch against NCCL's reduce-scatter
+    (torchrun, one rank per GPU).  Each rank reduces its shard of a 2 GB
+    symmetric buffer into a local FP32 buffer with aw4_reduce_multicast (the
+    FP32-state path of the ZeRO-2 step), BF16 and FP32; NCCL's
+    reduce_scatter_tensor runs on the same bytes.  10 launches after 3
+    warm-ups, max over ranks.  A rank's egress is its whole buffer: the
+    switch reads every rank's copy of a shard, the owner's own included."""
+    import ctypes
+
+    import torch.distributed as dist
+    import torch.distributed._symmetric_memory as symm_mem
+
+    from adamw4bit_b200 import _native as N
+    dev = torch.device("cuda", local)
+    if symm_mem.get_backend(dev) is None:
+        symm_mem.set_backend("CUDA")
+    lib = N.lib()
+    cur = torch.cuda.current_stream(dev)
+    reps = 10
+    for dt, n in ((torch.bfloat16, 1 << 30), (torch.float32, 1 << 29)):
+        buf = symm_mem.empty(n, dtype=dt, device=dev)
+        mc = int(symm_mem.rendezvous(buf, dist.group.WORLD).multicast_ptr)
+        buf.fill_(float(rank + 1))
+        shard, esz = n // world, buf.element_size()
+        res = torch.empty(shard, dtype=torch.float32, device=dev)
+
+        def reduce():
+            N.check(lib.aw4_reduce_multicast(ctypes.c_void_p(mc + rank * shard * esz),
+                                             N.DTYPE_CODES[dt], shard, 1.0,
+                                             ctypes.c_void_p(res.data_ptr()), local,
+                                             ctypes.c_void_p(cur.cuda_stream)),
+                    "aw4_reduce_multicast")
+        src = torch.full((n,), float(rank + 1), dtype=dt, device=dev)
+        dst = torch.empty(shard, dtype=dt, device=dev)
+
+        def timed(fn) -> float:
+            for _ in range(3):
+                fn()
+            barrier(world)
+            e0 = torch.cuda.Event(enable_timing=True)
+            e1 = torch.cuda.Event(enable_timing=True)
+            e0.record(cur)
+            for _ in range(reps):
+                fn()
+            e1.record(cur)
+            barrier(world)
+            return max_over_ranks(e0.elapsed_time(e1) / reps, world)
+        ms = timed(reduce)
+        correct = bool(torch.all(res == world * (world + 1) / 2).item())
+        ms_nccl = timed(lambda: dist.reduce_scatter_tensor(dst, src))
+        if rank == 0:
+            print(json.dumps({"probe": "ld_reduce", "dtype": str(dt).replace("torch.", ""),
+                              "world": world, "buffer_bytes": n * esz,
+                              "ld_reduce_ms": round(ms, 3),
+                              "shard_sums_in_gbs": round(shard * esz / ms / 1e6, 1),
+                              "egress_gbs": round(n * esz / ms / 1e6, 1),
+                              "nccl_reduce_scatter_ms": round(ms_nccl, 3),
+                              "correct": correct}), flush=True)
+        del buf, res, src, dst
+        barrier(world)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference", "reference-gpu", "reference-gpu-eager",
-                                       "reference-cpu", "reference-cpu-eager"],
-                    default="ours")
+                                       "reference-cpu", "reference-cpu-eager",
+                                       "probe-pcie", "probe-ld-reduce"],
+                    default="ours",
+                    help="probe-pcie / probe-ld-reduce: the copy and NVSwitch-reduction "
+                         "rates that bound e2e and the ZeRO-2 step (not bench lines)")
     ap.add_argument("--rounds", type=int, default=4,
                     help="rounds per step: one update launch each (and, at N>1, one gather)")
     ap.add_argument("--recipe", choices=["ze-eden", "zip-sr"], default="ze-eden",
@@ -782,8 +879,14 @@ def main():
         rank = int(os.environ.get("RANK", "0"))
         run_reference(args, rank, int(os.environ.get("WORLD_SIZE", "1")))
         return
+    if args.impl == "probe-pcie":
+        probe_pcie(args)
+        return
     rank, world, local = dist_setup(args.gpus)
     try:
+        if args.impl == "probe-ld-reduce":
+            probe_ld_reduce(args, rank, world, local)
+            return
         run_ours(args, rank, world, local)
     finally:
         if world > 1:
