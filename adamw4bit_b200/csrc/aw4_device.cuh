@@ -668,14 +668,19 @@ __device__ __forceinline__ int update_sr_from_index(const float* cb, const float
     return (u < p) ? l : r;
 }
 
-// Max over the 16 lanes of a block group (lanes 16h .. 16h+15 of a warp):
-// one warp reduction (Blackwell redux.f32) per group, NaN-propagating like
-// torch.max.
+// Max over the 16 lanes of a block group (lanes 16h .. 16h+15 of a warp),
+// NaN-propagating like torch.max: two full-warp reductions (Blackwell
+// redux.f32), one per group, to which the other group's lanes contribute
+// -inf.  The whole warp must call it.  One reduction per group with a
+// half-warp member mask gives the same values, but the two masks within one
+// warp cost convergence handling that made the step kernel 5 % slower.
 __device__ __forceinline__ float group_max16(float v) {
-    const unsigned mask = (threadIdx.x & 16) ? 0xFFFF0000u : 0x0000FFFFu;
-    float r;
-    asm volatile("redux.sync.max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(v), "r"(mask));
-    return r;
+    const bool hi = (threadIdx.x & 16) != 0;
+    const float lo_in = hi ? -INFINITY : v, hi_in = hi ? v : -INFINITY;
+    float r0, r1;
+    asm volatile("redux.sync.max.NaN.f32 %0, %1, 0xffffffff;" : "=f"(r0) : "f"(lo_in));
+    asm volatile("redux.sync.max.NaN.f32 %0, %1, 0xffffffff;" : "=f"(r1) : "f"(hi_in));
+    return hi ? r1 : r0;
 }
 
 }  // namespace aw4
