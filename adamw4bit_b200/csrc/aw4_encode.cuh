@@ -167,18 +167,14 @@ __device__ __forceinline__ void sr_table(const GroupCtx& g, const SmemScheme& S,
     const int j = g.j;
     const float fj = precond24(sc, S.cb[j], bias, rbias, eps);
     const float fprev = __shfl_up_sync(0xffffffffu, fj, 1, 16);
-    float dl = 1.0f, y = 0.0f;
-    int rc = max(j, floor_code);
-    if (j >= 1) {
-        const int lc = max(j - 1, floor_code);
-        const float den = fsub(fprev, fj);   // 2^24 (f[l] - f[r]), exactly
-        if (fsub(S.cb[j], S.cb[j - 1]) > 0.0f && den > 0.0f) {
-            dl = fmul(den, 0x1p-24f);
-            if (lc != rc) y = rcp_nr(dl);
-        } else {
-            rc = lc;
-        }
-    }
+    // branch-free: lane 0 has no interval below it (its fprev is its own fj)
+    const int rc0 = max(j, floor_code), lc = max(j - 1, floor_code);
+    const float den = fsub(fprev, fj);   // 2^24 (f[l] - f[r]), exactly
+    const bool interval = j >= 1 && fsub(S.cb[j], S.cb[max(j - 1, 0)]) > 0.0f && den > 0.0f;
+    const float dl = interval ? fmul(den, 0x1p-24f) : 1.0f;
+    const float yr = rcp_nr(dl);        // dl is 1 or a normal divisor in rcp_nr's exact range
+    const float y = (interval && lc != rc0) ? yr : 0.0f;
+    const int rc = (j >= 1 && !interval) ? lc : rc0;
     g.sr_tab[j] = make_float4(fj, dl, y, __int_as_float(rc));
     if (j == 15) g.sr_tab[16] = make_float4(fj, 1.0f, 0.0f, __int_as_float(15));
 }
