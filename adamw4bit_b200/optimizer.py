@@ -33,7 +33,6 @@ from . import _native as N
 from .quantization import (
     SCHEMES,
     QuantState,
-    default_block_size,
     pack_4bit_codes,
     prepared,
     scheme_info,
