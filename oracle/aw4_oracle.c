@@ -397,6 +397,44 @@ int aw4o_step(const aw4o_step_cfg* c, void* param, const void* grad, int64_t n,
     return 0;
 }
 
+/* Step of one tensor with an FP32 first moment next to a quantized second
+ * moment (m1_quant_scheme="fp32": adamw.py:510-521 resolves each moment's
+ * scheme separately, and an FP32 moment is a plain float32 tensor,
+ * adamw.py:830-833).  m1 is updated in place; m2 is decoded, updated and
+ * re-encoded exactly as in aw4o_step.  cfg->cb1 and m1_mode are unused. */
+int aw4o_step_fp32_m1(const aw4o_step_cfg* c, void* param, const void* grad, int64_t n,
+                      float* m1, uint8_t* m2_packed, float* m2_scales, const float* m2_draws) {
+    if (n % AW4O_BLOCK) return -1;
+    aw4o_scalars s = make_scalars(c);
+    aw4o_codec q2 = {c->cb2, c->m2_mode, c->m2_zero_floor, c->eden, s.sr_bias, s.eps};
+    int64_t nb = n / AW4O_BLOCK;
+#pragma omp parallel for schedule(static)
+    for (int64_t b = 0; b < nb; ++b) {
+        float m2[AW4O_BLOCK], u2[AW4O_BLOCK];
+        uint8_t c2[AW4O_BLOCK];
+        int64_t base = b * AW4O_BLOCK;
+        float s2 = m2_scales[b];
+        for (int j = 0; j < AW4O_BLOCK; ++j) {
+            int64_t i = base + j;
+            int k2 = (m2_packed[i >> 1] >> ((i & 1) * 4)) & 15;
+            m2[j] = c->cb2[k2] * s2;      /* dequantize (quantization.py:999) */
+            float g = load_elem(grad, c->grad_dtype, i);
+            float p = load_elem(param, c->param_dtype, i);
+            adamw_elem(&s, c->param_dtype, g, &m1[i], &m2[j], &p);
+            store_elem(param, c->param_dtype, i, p);
+        }
+        if (c->m2_mode != AW4O_RTN)
+            for (int j = 0; j < AW4O_BLOCK; ++j)
+                u2[j] = m2_draws ? m2_draws[base + j]
+                                 : aw4o_philox_uniform(c->m2_key, (uint32_t)c->step, c->ordinal,
+                                                       (uint64_t)(c->elem_offset + base + j));
+        quantize_block(&q2, m2, u2, c2, &m2_scales[b]);
+        for (int j = 0; j < AW4O_BLOCK; j += 2)
+            m2_packed[(base + j) >> 1] = (uint8_t)(c2[j] | (c2[j + 1] << 4));
+    }
+    return 0;
+}
+
 /* Step of one tensor whose moments stay FP32 because it is not eligible for
  * quantized state (adamw.py:807-817: numel < 4096 or not a block multiple). */
 int aw4o_step_fp32_state(const aw4o_step_cfg* c, void* param, const void* grad, int64_t n,

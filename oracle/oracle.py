@@ -109,6 +109,7 @@ def lib() -> ctypes.CDLL:
         vp, i64, i32, f64 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_double
         L.aw4o_step.argtypes = [ctypes.POINTER(StepCfg), vp, vp, i64, vp, vp, vp, vp, vp, vp]
         L.aw4o_step_fp32_state.argtypes = [ctypes.POINTER(StepCfg), vp, vp, i64, vp, vp]
+        L.aw4o_step_fp32_m1.argtypes = [ctypes.POINTER(StepCfg), vp, vp, i64, vp, vp, vp, vp]
         L.aw4o_quantize.argtypes = [vp, i64, vp, i32, i32, i32, vp, f64, f64, vp, vp]
         L.aw4o_dequantize.argtypes = [vp, vp, i64, vp, vp]
         L.aw4o_dequantize.restype = None
@@ -197,8 +198,9 @@ def stream_key(seed: int, offset: int) -> int:
 def make_cfg(*, m1_scheme: str, m2_scheme: str, eden: bool, lr: float, betas, eps: float,
              weight_decay: float, step: int, param_dtype: int = F32, grad_dtype: int = F32,
              m1_key: int = 0, m2_key: int = 0, ordinal: int = 0, elem_offset: int = 0):
-    cb1, mode1, _ = SCHEMES[m1_scheme]
     cb2, mode2, floor2 = SCHEMES[m2_scheme]
+    # an FP32 first moment (step_fp32_m1) has no codebook: m1 fields unused
+    cb1, mode1, _ = (cb2, RTN, 0) if m1_scheme == "fp32" else SCHEMES[m1_scheme]
     cfg = StepCfg(param_dtype, grad_dtype, mode1, mode2, floor2, int(eden),
                   int(m2_scheme in NEXT_BIAS), cb1.ctypes.data, cb2.ctypes.data,
                   lr, betas[0], betas[1], eps, weight_decay, step, m1_key, m2_key, ordinal,
@@ -217,6 +219,18 @@ def step(cfg: StepCfg, param: np.ndarray, grad: np.ndarray, m1_codes: np.ndarray
     rc = lib().aw4o_step(ctypes.byref(cfg), _ptr(param), _ptr(grad), n, _ptr(m1_codes),
                          _ptr(m1_scales), _ptr(m2_codes), _ptr(m2_scales), _ptr(m1_draws),
                          _ptr(m2_draws))
+    assert rc == 0
+
+
+def step_fp32_m1(cfg: StepCfg, param: np.ndarray, grad: np.ndarray, m1: np.ndarray,
+                 m2_codes: np.ndarray, m2_scales: np.ndarray,
+                 m2_draws: np.ndarray | None = None) -> None:
+    """In-place step of one tensor with an FP32 m1 (float32[n]) next to a
+    packed 4-bit m2 (cfg made with m1_scheme="fp32")."""
+    for a in (param, grad, m1, m2_codes, m2_scales):
+        assert a.flags["C_CONTIGUOUS"]
+    rc = lib().aw4o_step_fp32_m1(ctypes.byref(cfg), _ptr(param), _ptr(grad), param.size,
+                                 _ptr(m1), _ptr(m2_codes), _ptr(m2_scales), _ptr(m2_draws))
     assert rc == 0
 
 

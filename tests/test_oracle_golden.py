@@ -154,14 +154,16 @@ def test_oracle_full_size_trajectory_matches_reference(name):
     run_oracle_trajectory(meta, on_step=check)
 
 
-@pytest.mark.parametrize("name", ["nf4_lookahead", "nf4_nextbc", "nf4_lin4_fp32read"])
-def test_oracle_fp32read_scheme_pairs_match_reference(name):
-    """The fp32-read update-SR m2 schemes next to an nf4 m1, 6 steps of the
-    reference's QuantizedAdamW (tests/golden/make_golden_configs.py):
-    dyn4_lookahead_sr and its nextbc alias store against the next step's bias
-    correction c_{t+1}, lin4_upd_sr_fp32read against c_t (adamw.py:112-116,
-    655-683).  The oracle, fed the reference's m2 draws, must reproduce every
-    digest of codes, scales and FP32 moments."""
+@pytest.mark.parametrize("name", ["nf4_lookahead", "nf4_nextbc", "nf4_lin4_fp32read",
+                                  "fp32m1_zipsr", "fp32m1_zeeden", "fp32m1_lookahead"])
+def test_oracle_scheme_pairs_match_reference(name):
+    """Scheme pairs through the reference's QuantizedAdamW, 6 steps
+    (tests/golden/make_golden_configs.py): the fp32-read update-SR m2 schemes
+    next to an nf4 m1 (dyn4_lookahead_sr and its nextbc alias store against
+    the next step's bias correction c_{t+1}, lin4_upd_sr_fp32read against
+    c_t; adamw.py:112-116, 655-683), and an FP32 m1 next to a 4-bit m2
+    (adamw.py:510-521).  The oracle, fed the reference's m2 draws, must
+    reproduce every digest of codes, scales and FP32 moments."""
     import hashlib
 
     from tests import synth as S
@@ -171,28 +173,39 @@ def test_oracle_fp32read_scheme_pairs_match_reference(name):
     shapes = [tuple(s) for s in meta["shapes"]]
     params = [S.init_param(s, i, torch.float32, "cpu").numpy().reshape(-1).copy()
               for i, s in enumerate(shapes)]
+    fp32_m1 = meta["m1_scheme"] == "fp32"
     state = []
     for p in params:
         if G.eligible(p.size):
-            c1, s1 = O.init_zero(meta["m1_scheme"], p.size)
             c2, s2 = O.init_zero(meta["m2_scheme"], p.size, eden=meta["eden"])
-            state.append({"m1_code": c1, "m1_absmax": s1, "m2_code": c2, "m2_absmax": s2})
+            if fp32_m1:
+                state.append({"m1": np.zeros(p.size, np.float32), "m2_code": c2, "m2_absmax": s2})
+            else:
+                c1, s1 = O.init_zero(meta["m1_scheme"], p.size)
+                state.append({"m1_code": c1, "m1_absmax": s1, "m2_code": c2, "m2_absmax": s2})
         else:
             state.append({"m1": np.zeros(p.size, np.float32), "m2": np.zeros(p.size, np.float32)})
-    gen = torch.Generator().manual_seed((meta["quant_rng_seed"] + G.M2_OFFSET) % ((1 << 63) - 1))
+    sr = O.SCHEMES[meta["m2_scheme"]][1] != O.RTN
+    seed = meta["quant_rng_seed"]
+    gen = torch.Generator().manual_seed((seed + G.M2_OFFSET) % ((1 << 63) - 1)) if sr else None
     for t in range(1, meta["steps"] + 1):
         cfg = O.make_cfg(m1_scheme=meta["m1_scheme"], m2_scheme=meta["m2_scheme"],
                          eden=meta["eden"], lr=1e-3, betas=(0.9, 0.95), eps=1e-8,
                          weight_decay=0.1, step=t, param_dtype=O.F32, grad_dtype=O.F32)
         for i, (p, st) in enumerate(zip(params, state)):
             g = S.grad(shapes[i], i, t, meta["grad_std"], torch.float32, "cpu").numpy().reshape(-1)
-            if "m1_code" in st:
-                rows = (p.size // 128, 128)
-                if t == 1:
-                    torch.rand(rows, generator=gen)                 # zero-state init
-                d2 = torch.rand(rows, generator=gen).numpy().reshape(-1).copy()
-                O.step(cfg, p, g.copy(), st["m1_code"], st["m1_absmax"], st["m2_code"],
-                       st["m2_absmax"], None, d2)
+            if "m2_code" in st:
+                d2 = None
+                if gen is not None:
+                    rows = (p.size // 128, 128)
+                    if t == 1:
+                        torch.rand(rows, generator=gen)             # zero-state init
+                    d2 = torch.rand(rows, generator=gen).numpy().reshape(-1).copy()
+                if fp32_m1:
+                    O.step_fp32_m1(cfg, p, g.copy(), st["m1"], st["m2_code"], st["m2_absmax"], d2)
+                else:
+                    O.step(cfg, p, g.copy(), st["m1_code"], st["m1_absmax"], st["m2_code"],
+                           st["m2_absmax"], None, d2)
             else:
                 O.step_fp32_state(cfg, p, g.copy(), st["m1"], st["m2"])
         hs = {k: hashlib.sha256() for k in ("m1_code", "m1_absmax", "m2_code", "m2_absmax",
